@@ -1,0 +1,399 @@
+"""Benchmark: HBM GB/s of musapy's broadcast add and axis sums on B200.
+
+Workload: a float32 (65536, 32768) array, uniform[-1, 1)
+from numpy PCG64 seed 5, sharded on axis 0 across the GPUs of one node (one
+process per GPU), and a replicated (32768,) row vector drawn after it. One
+step is the hot path over the whole array:
+
+    y   = x + row                 broadcast add           (local)
+    r   = sum(y, axis=1)          axis sum                (local)
+    s,m = sum(x), mean(x)         full reduction          (one NCCL all_reduce)
+    i   = argmax(x)               full arg reduction      (one NCCL all_gather)
+
+`value` = algorithmic bytes of all ranks / step time (each input read once,
+each output written once), max over ranks; `e2e` is the same metric with the
+step's input copied from pinned host memory and its results copied back
+inside the timed region. Total work is fixed as N grows (strong scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ROWS, COLS, SEED = 1 << 16, 1 << 15, 5
+METRIC = "HBM GB/s & % of peak: broadcast add and axis-sum at 1/2/4/8 B200"
+WORKLOAD = ("config5: f32 (65536, 32768) uniform[-1,1) seed 5 sharded on axis 0 + replicated (32768,) row; "
+            "step = broadcast add -> sum(axis=1) -> sum/mean(all) -> argmax(all)")
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def shard_rows(n_rows: int, world: int, rank: int):
+    base, extra = divmod(n_rows, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def gen_rows(r0: int, r1: int, cols: int, out=None):
+    """Rows [r0, r1) of the config-5 matrix from one PCG64 stream (seed 5),
+    generated chunk by chunk: each float32 draw consumes half of a 64-bit
+    PCG64 step, so the stream is advanced to row r0 directly."""
+    import numpy as np
+
+    bg = np.random.PCG64(SEED)
+    bg.advance((r0 * cols) // 2)
+    rng = np.random.Generator(bg)
+    n = r1 - r0
+    if out is None:
+        out = np.empty((n, cols), dtype=np.float32)
+    chunk = max(1, (1 << 24) // cols)
+    for i in range(0, n, chunk):
+        j = min(n, i + chunk)
+        out[i:j] = rng.random((j - i, cols), dtype=np.float32) * 2 - 1
+    return out
+
+
+def gen_row_vector(rows: int, cols: int):
+    import numpy as np
+
+    bg = np.random.PCG64(SEED)
+    bg.advance((rows * cols) // 2)
+    return np.random.Generator(bg).random(cols, dtype=np.float32) * 2 - 1
+
+
+def step_bytes(rows: int, cols: int) -> dict:
+    n = rows * cols * 4
+    return {
+        "add": n + cols * 4 + n,          # read x, read row, write y
+        "sum_axis1": n + rows * 4,        # read y, write row sums
+        "sum_all": n,                     # read x (sum and mean share the pass)
+        "argmax": n,                      # read x
+    }
+
+
+def measured_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic() -> dict:
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary, if one exists (profiles/ncu_traffic.json)."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self) -> None:
+        self.proc = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpus) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        mhz, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+            except ValueError:
+                continue
+            if idx not in gpus:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                pass
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# --------------------------------------------------------------- CPU legs
+def cpu_sample(rows: int, cols: int, threads: int, steps: int, warmup: int) -> dict:
+    """The oracle port (the reference CPU path restated) on a bounded sample:
+    the first `rows` rows of the same matrix, the same step."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    O.build()
+    O.set_threads(threads)
+    x = gen_rows(0, rows, cols)
+    row = gen_row_vector(ROWS, cols)
+    b = step_bytes(rows, cols)
+
+    def one():
+        y = O.binary("add", x, row)
+        O.reduce("sum", y, axis=1)
+        O.reduce("sum", x, None)
+        O.reduce("mean", x, None)
+        O.reduce("argmax", x, None)
+
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = (time.perf_counter() - t0) / steps
+    total = sum(b.values())
+    return {"value": total / dt / 1e9, "unit": "GB/s", "cores": threads, "seconds_per_step": dt,
+            "sample": f"first {rows} of {ROWS} rows ({rows * cols} f32 elements), same step, "
+                      f"{'1 thread (scalar port)' if threads == 1 else f'{threads} OpenMP threads'}"}
+
+
+def run_reference(args) -> None:
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    O.build()
+    threads = O.max_threads()
+    rows = args.sample_rows
+    r = cpu_sample(rows, COLS, threads, max(1, args.steps), max(0, args.warmup))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(r["seconds_per_step"] * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows_sampled": rows, "cols": COLS},
+        "cpu_baseline": {"value": round(r["value"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": round(r["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU leg
+def run_b200(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+    torch.cuda.set_device(local)
+    import datetime
+
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    import musapy_b200 as ms
+    from musapy_b200 import shard as sh
+
+    rows, cols = args.rows, COLS
+    r0, r1 = shard_rows(rows, world, rank)
+    nloc = r1 - r0
+    dev = local
+    stream = torch.cuda.current_stream(dev)
+
+    # host data (pinned) and the device copies
+    host_x = torch.empty((nloc, cols), dtype=torch.float32, pin_memory=True)
+    gen_rows(r0, r1, cols, out=host_x.numpy())
+    host_row = torch.from_numpy(gen_row_vector(rows, cols)).pin_memory()
+    x = ms.empty((nloc, cols), "f32", dev)
+    row = ms.empty((cols,), "f32", dev)
+    x.torch().copy_(host_x, non_blocking=True)
+    row.torch().copy_(host_row, non_blocking=True)
+    y = ms.empty((nloc, cols), "f32", dev)
+    rowsum = ms.empty((nloc,), "f32", dev)
+    xs = sh.ShardedArray(x, (rows, cols), r0)
+    ys = sh.ShardedArray(y, (rows, cols), r0)
+    sc = sh._SumCombine(dev, ms.float32)
+    ac = sh._ArgCombine(dev, world)
+    torch.cuda.synchronize()
+
+    nev = 5
+
+    def step(evs=None):
+        if evs is not None:
+            evs[0].record(stream)
+        sh.add(xs, row, out=y)
+        if evs is not None:
+            evs[1].record(stream)
+        sh.sum_axis(ys, 1, out=rowsum)
+        if evs is not None:
+            evs[2].record(stream)
+        sh.sum_all(xs, sc)
+        if evs is not None:
+            evs[3].record(stream)
+        sh.argreduce_all(xs, True, ac)
+        if evs is not None:
+            evs[4].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    if local == 0:
+        clocks.start()
+        time.sleep(0.4)
+    torch.cuda.synchronize()
+    barrier()
+    launches0 = ms._lib.launch_count()
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(evs[k])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = ms._lib.launch_count() - launches0
+    barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    op_ms = {name: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs)
+             for i, name in enumerate(["add", "sum_axis1", "sum_all", "argmax"])}
+    clk = clocks.stop(set(range(world))) if local == 0 else None
+
+    # e2e through the public API: host input -> device, step, results -> host
+    host_rowsum = torch.empty((nloc,), dtype=torch.float32, pin_memory=True)
+    host_scalars = torch.empty(3, dtype=torch.float64, pin_memory=True)
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        x.torch().copy_(host_x, non_blocking=True)
+        row.torch().copy_(host_row, non_blocking=True)
+        step()
+        host_rowsum.copy_(rowsum.torch(), non_blocking=True)
+        host_scalars[0:1].copy_(sc.sum_out.torch().reshape(1), non_blocking=True)
+        host_scalars[1:2].copy_(sc.mean_out.torch().reshape(1), non_blocking=True)
+        host_scalars[2:3].copy_(ac.index.torch().reshape(1), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    h2d = nloc * cols * 4 + cols * 4
+    d2h = nloc * 4 + 3 * 8
+
+    # max over ranks of the step time, total bytes over ranks
+    b_local = step_bytes(nloc, cols)
+    vals = torch.tensor([ms_total / args.steps, e2e_ms], dtype=torch.float64, device=f"cuda:{dev}")
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    t_step, t_e2e = float(vals[0]), float(vals[1])
+    total_bytes = sum(step_bytes(rows, cols).values())
+    value = total_bytes / (t_step * 1e-3) / 1e9
+    e2e_value = total_bytes / (t_e2e * 1e-3) / 1e9
+
+    peak, peak_kind = measured_peak()
+    add_bytes = b_local["add"]
+    achieved = add_bytes / (op_ms["add"] * 1e-3) / 1e9
+    tr = ncu_traffic()
+    traffic = None
+    if tr.get("kernel_bytes_per_launch") and tr.get("rows_per_launch"):
+        traffic = int(tr["kernel_bytes_per_launch"] * (nloc / tr["rows_per_launch"]))
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(args.sample_rows, cols, 1, 1, 0)
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": round(t_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows": rows, "cols": cols, "parallelism": f"axis0-shard{world}",
+                   "global_batch": rows, "l2": "inputs 8 GiB > 126 MB L2: no flush needed",
+                   "per_op_ms": {k: round(v, 4) for k, v in op_ms.items()},
+                   "per_op_gbs": {k: round(b_local[k] / (v * 1e-3) / 1e9, 1) for k, v in op_ms.items()},
+                   "per_op_frac": {k: round(b_local[k] / (v * 1e-3) / 1e9 / peak, 4) for k, v in op_ms.items()}},
+        "roofline": {"bound": "hbm", "kernel": "k_ew_rows (broadcast add)", "achieved": round(achieved, 1),
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "bytes_per_launch": add_bytes, "traffic": traffic},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
+                "d2h_bytes_per_step": d2h * world, "ms_per_step": round(t_e2e, 3)},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = {"value": round(cpu["value"], 4), "unit": "GB/s", "cores": cpu["cores"],
+                                "kind": "port", "sample": cpu["sample"]}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--rows", type=int, default=ROWS, help="global rows (default: config 5)")
+    ap.add_argument("--sample-rows", type=int, default=2048, help="rows of the CPU sample")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

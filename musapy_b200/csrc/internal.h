@@ -1,0 +1,36 @@
+// Internal host helpers: error reporting and device queries.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "mpb_types.h"
+
+namespace mpb {
+
+// Records a message for mpb_last_error() (thread-local) and returns `code`.
+int fail(int code, const char* fmt, ...);
+// MPB_OK when `e` is cudaSuccess, otherwise records the CUDA error.
+int cuda_check(cudaError_t e, const char* what);
+// Checks cudaGetLastError() after a launch.
+int launch_check(const char* what);
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
+struct EwReq {
+  int op;
+  int ndim;
+  const int64_t* shape;
+  const void* a;
+  int a_dt;
+  const int64_t* a_st;
+  const void* b;  // null for unary ops
+  int b_dt;
+  const int64_t* b_st;
+  void* out;  // C-contiguous with `shape`
+  int out_dt;
+  int compute_dt;
+  double p0, p1;  // clamp bounds / fill value
+};
+
+int ew_run(const EwReq& r, cudaStream_t stream);
+
+}  // namespace mpb

@@ -1,0 +1,444 @@
+// Inclusive prefix sum (cumsum) along one axis, for sm_100a.
+//
+// Replaces the 3-to-5 launch Blelloch ladder of kernels/reduction.mu:557-820
+// and :1723-1776 (block scan -> scan of block sums -> add prefix) and lifts its
+// 256^3 length limit (rust/musapy-ops/src/op_builder.rs:3291-3300):
+//   ROWS      many rows along a unit-stride axis: one CTA per row walks the row
+//             in 4096-element tiles, carrying the running total; loads are
+//             warp-striped 16-byte vectors, the scan is thread-sequential over
+//             each vector, a warp shuffle scan across lanes and a shared-memory
+//             scan across warps;
+//   LOOKBACK  few long rows (axis=None included): single pass, tiles taken in
+//             order from an atomic ticket, each tile publishes its aggregate
+//             and inclusive prefix and looks back over its predecessors
+//             (Merrill & Garland, "Single-pass Parallel Prefix Scan with
+//             Decoupled Look-back", NVIDIA 2016). Every wait is bounded: on
+//             expiry the kernel records MPB_ERR_TIMEOUT in a status word and
+//             continues, so it always terminates;
+//   COLS      axis with a non-unit stride and unit-stride columns: one thread per
+//             column adds along the axis in index order, the same additions in
+//             the same order as the CPU loop (op_builder.rs:3640-3688);
+//   GEN       anything else: one thread per row, sequential.
+#include <stdint.h>
+#include "common.cuh"
+#include "internal.h"
+#include "plan.h"
+#include "reduce.h"
+
+namespace mpb {
+namespace {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanJ = 4;  // vector rows per warp per tile
+
+template <class Acc> MPB_D Acc sadd(Acc a, Acc b) { return a + b; }
+MPB_D int64_t sadd(int64_t a, int64_t b) { return (int64_t)((uint64_t)a + (uint64_t)b); }
+
+template <class T> MPB_D T shfl_up(T x, int o);
+template <> MPB_D float shfl_up<float>(float x, int o) { return __shfl_up_sync(0xffffffffu, x, o); }
+template <> MPB_D double shfl_up<double>(double x, int o) { return __shfl_up_sync(0xffffffffu, x, o); }
+template <> MPB_D int64_t shfl_up<int64_t>(int64_t x, int o) { return __shfl_up_sync(0xffffffffu, (long long)x, o); }
+template <class T> MPB_D T shfl_idx(T x, int l);
+template <> MPB_D float shfl_idx<float>(float x, int l) { return __shfl_sync(0xffffffffu, x, l); }
+template <> MPB_D double shfl_idx<double>(double x, int l) { return __shfl_sync(0xffffffffu, x, l); }
+template <> MPB_D int64_t shfl_idx<int64_t>(int64_t x, int l) { return __shfl_sync(0xffffffffu, (long long)x, l); }
+
+// Inclusive warp scan (Kogge-Stone over 32 lanes).
+template <class Acc>
+MPB_D Acc warp_incl_scan(Acc v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    Acc u = shfl_up<Acc>(v, o);
+    if (lane >= o) v = sadd(v, u);
+  }
+  return v;
+}
+
+struct ScanDev {
+  int K;
+  int64_t M, L;
+  int64_t ks[kMaxCollapsed], kin[kMaxCollapsed], kout[kMaxCollapsed];
+  int64_t sa, so;  // axis strides of input and output
+};
+
+MPB_D void row_offsets(const ScanDev& g, int64_t o, int64_t& oi, int64_t& oo) {
+  oi = 0;
+  oo = 0;
+  for (int d = g.K - 1; d >= 0; --d) {
+    const int64_t c = o % g.ks[d];
+    o /= g.ks[d];
+    oi += c * g.kin[d];
+    oo += c * g.kout[d];
+  }
+}
+
+// Scan one tile of up to kTile elements starting at element `t0` of a row.
+// Returns the tile total (block-uniform). `carry` is added to every output.
+template <class In, class Acc>
+struct Tile {
+  static constexpr int VEC = 16 / sizeof(Acc);
+  static constexpr int kWarpElems = kScanJ * 32 * VEC;
+  static constexpr int kTile = (kScanThreads / 32) * kWarpElems;
+};
+
+template <class In, class Acc>
+MPB_D Acc scan_tile(const In* __restrict__ in, Acc* __restrict__ out, int64_t n, bool vec_ok, Acc carry,
+                    Acc* s_warp /* [8] */, bool publish_only_total, Acc* total_out) {
+  using TL = Tile<In, Acc>;
+  constexpr int VEC = TL::VEC;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  Acc v[kScanJ][VEC];
+  const int64_t wbase = (int64_t)warp * TL::kWarpElems;
+  const bool full = vec_ok && (n >= TL::kTile);
+#pragma unroll
+  for (int j = 0; j < kScanJ; ++j) {
+    const int64_t e = wbase + (int64_t)j * 32 * VEC + (int64_t)lane * VEC;
+    if (full) {
+      const uint4 w = ld_stream16(in + e);
+      const Acc* p = reinterpret_cast<const Acc*>(&w);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[j][k] = p[k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[j][k] = (e + k < n) ? cvt<Acc>(in[e + k]) : Acc(0);
+    }
+  }
+  // thread-sequential over each vector, warp scan over lanes, rows in order
+  Acc run = Acc(0);
+#pragma unroll
+  for (int j = 0; j < kScanJ; ++j) {
+#pragma unroll
+    for (int k = 1; k < VEC; ++k) v[j][k] = sadd(v[j][k], v[j][k - 1]);
+    const Acc tot = v[j][VEC - 1];
+    const Acc incl = warp_incl_scan<Acc>(tot, lane);
+    Acc excl = shfl_up<Acc>(incl, 1);
+    if (lane == 0) excl = Acc(0);
+    const Acc pre = sadd(run, excl);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[j][k] = sadd(v[j][k], pre);
+    run = sadd(run, shfl_idx<Acc>(incl, 31));
+  }
+  // cross-warp scan of warp totals
+  __syncthreads();
+  if (lane == 0) s_warp[warp] = run;
+  __syncthreads();
+  Acc wpre = Acc(0), total = Acc(0);
+  for (int w = 0; w < kScanThreads / 32; ++w) {
+    const Acc t = s_warp[w];
+    if (w < warp) wpre = sadd(wpre, t);
+    total = sadd(total, t);
+  }
+  if (total_out) *total_out = total;
+  if (publish_only_total) return total;
+  const Acc add = sadd(carry, wpre);
+#pragma unroll
+  for (int j = 0; j < kScanJ; ++j) {
+    const int64_t e = wbase + (int64_t)j * 32 * VEC + (int64_t)lane * VEC;
+    if (full) {
+      uint4 w;
+      Acc* p = reinterpret_cast<Acc*>(&w);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) p[k] = sadd(v[j][k], add);
+      st_stream16(out + e, w);
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k)
+        if (e + k < n) out[e + k] = sadd(v[j][k], add);
+    }
+  }
+  return total;
+}
+
+// ----------------------------------------------------------------- ROWS
+template <class In, class Acc>
+__global__ void __launch_bounds__(kScanThreads) k_scan_rows(const In* __restrict__ a, Acc* __restrict__ out,
+                                                             ScanDev g, int vec_ok) {
+  using TL = Tile<In, Acc>;
+  __shared__ Acc s_warp[kScanThreads / 32];
+  for (int64_t o = blockIdx.x; o < g.M; o += gridDim.x) {
+    int64_t oi, oo;
+    row_offsets(g, o, oi, oo);
+    Acc carry = Acc(0);
+    for (int64_t t0 = 0; t0 < g.L; t0 += TL::kTile) {
+      Acc total;
+      scan_tile<In, Acc>(a + oi + t0, out + oo + t0, g.L - t0, vec_ok != 0, carry, s_warp, false, &total);
+      carry = sadd(carry, total);
+    }
+  }
+}
+
+// ------------------------------------------------------------- LOOKBACK
+// Scratch layout: [u32 ticket][i32 status][pad 8] then per tile:
+// flags (i32, 0 = none, 1 = aggregate ready, 2 = inclusive prefix ready),
+// then aggregates (Acc), then inclusive prefixes (Acc).
+constexpr int64_t kSpinLimit = 1 << 22;  // polls per predecessor before giving up
+
+template <class Acc>
+MPB_D int wait_flag(volatile int* f, int* status) {
+  int v = *f;
+  int64_t spins = 0;
+  unsigned ns = 32;
+  while (v == 0) {
+    if (++spins > kSpinLimit) {
+      atomicOr(status, 1 << MPB_ERR_TIMEOUT);
+      return 0;
+    }
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+    v = *f;
+  }
+  return v;
+}
+
+template <class In, class Acc>
+__global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __restrict__ a, Acc* __restrict__ out,
+                                                                 ScanDev g, int vec_ok, char* __restrict__ scratch,
+                                                                 int64_t tiles_per_row) {
+  using TL = Tile<In, Acc>;
+  __shared__ Acc s_warp[kScanThreads / 32];
+  __shared__ uint32_t s_ticket;
+  __shared__ Acc s_prefix;
+  unsigned* ticket = reinterpret_cast<unsigned*>(scratch);
+  int* status = reinterpret_cast<int*>(scratch + 4);
+  const int64_t ntiles = g.M * tiles_per_row;
+  int* flags = reinterpret_cast<int*>(scratch + 16);
+  Acc* aggs = reinterpret_cast<Acc*>(scratch + 16 + ((ntiles * 4 + 15) / 16) * 16);
+  Acc* incs = aggs + ntiles;
+  if (threadIdx.x == 0) s_ticket = atomicAdd(ticket, 1u);
+  __syncthreads();
+  const int64_t tid = s_ticket;
+  if (tid >= ntiles) return;
+  const int64_t row = tid / tiles_per_row;
+  const int64_t t = tid - row * tiles_per_row;
+  int64_t oi, oo;
+  row_offsets(g, row, oi, oo);
+  const int64_t t0 = t * TL::kTile;
+  const In* in = a + oi + t0;
+  Acc* dst = out + oo + t0;
+  const int64_t n = g.L - t0;
+  // pass 1: tile total only (values stay in registers of scan_tile's caller
+  // is not possible across the wait, so the tile is scanned once the prefix
+  // is known; the total comes from the same loads)
+  Acc total;
+  scan_tile<In, Acc>(in, dst, n, vec_ok != 0, Acc(0), s_warp, true, &total);
+  if (threadIdx.x == 0) {
+    volatile int* vf = flags;
+    if (t == 0) {
+      incs[tid] = total;
+      __threadfence();
+      vf[tid] = 2;
+      s_prefix = Acc(0);
+    } else {
+      aggs[tid] = total;
+      __threadfence();
+      vf[tid] = 1;
+      Acc excl = Acc(0);
+      for (int64_t p = tid - 1; p >= tid - t; --p) {
+        const int f = wait_flag<Acc>(vf + p, status);
+        __threadfence();
+        if (f == 2) {
+          excl = sadd(excl, *(volatile Acc*)(incs + p));
+          break;
+        }
+        if (f == 0) break;  // the wait gave up (recorded in the status word): stop looking back
+        excl = sadd(excl, *(volatile Acc*)(aggs + p));
+      }
+      incs[tid] = sadd(excl, total);
+      __threadfence();
+      vf[tid] = 2;
+      s_prefix = excl;
+    }
+  }
+  __syncthreads();
+  const Acc carry = s_prefix;
+  scan_tile<In, Acc>(in, dst, n, vec_ok != 0, carry, s_warp, false, nullptr);
+}
+
+// ----------------------------------------------------------------- COLS
+// One thread per column (innermost kept dim unit-stride in and out).
+template <class In, class Acc>
+__global__ void __launch_bounds__(kScanThreads) k_scan_cols(const In* __restrict__ a, Acc* __restrict__ out,
+                                                             ScanDev g) {
+  const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t o = gt; o < g.M; o += gs) {
+    int64_t oi, oo;
+    row_offsets(g, o, oi, oo);
+    Acc acc = Acc(0);
+    constexpr int UNR = 8;
+    int64_t k = 0;
+    for (; k + UNR <= g.L; k += UNR) {
+      Acc v[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) v[u] = cvt<Acc>(a[oi + (k + u) * g.sa]);
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        acc = sadd(acc, v[u]);
+        out[oo + (k + u) * g.so] = acc;
+      }
+    }
+    for (; k < g.L; ++k) {
+      acc = sadd(acc, cvt<Acc>(a[oi + k * g.sa]));
+      out[oo + k * g.so] = acc;
+    }
+  }
+}
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct ScanPlan {
+  ScanDev g;
+  int kind;  // 0 rows, 1 lookback, 2 cols/gen (sequential per thread)
+  int vec_ok;
+  int64_t tiles_per_row;
+};
+
+template <class In, class Acc>
+ScanPlan scan_plan(const ScanReq& r) {
+  ScanPlan pl;
+  ScanDev& g = pl.g;
+  int64_t out_st[MPB_MAX_DIMS];
+  int64_t acc = 1;
+  for (int i = r.ndim - 1; i >= 0; --i) {
+    out_st[i] = acc;
+    acc *= r.shape[i];
+  }
+  g.L = r.shape[r.axis];
+  g.sa = r.strides[r.axis];
+  g.so = out_st[r.axis];
+  g.M = 1;
+  int64_t ks[MPB_MAX_DIMS], ki[MPB_MAX_DIMS], ko[MPB_MAX_DIMS];
+  int K = 0;
+  for (int d = 0; d < r.ndim; ++d) {
+    if (d == r.axis) continue;
+    g.M *= r.shape[d];
+    if (r.shape[d] == 1) continue;
+    if (K > 0 && ki[K - 1] == r.strides[d] * r.shape[d] && ko[K - 1] == out_st[d] * r.shape[d]) {
+      ks[K - 1] *= r.shape[d];
+      ki[K - 1] = r.strides[d];
+      ko[K - 1] = out_st[d];
+    } else {
+      ks[K] = r.shape[d];
+      ki[K] = r.strides[d];
+      ko[K] = out_st[d];
+      ++K;
+    }
+  }
+  g.K = K;
+  for (int d = 0; d < K && d < kMaxCollapsed; ++d) {
+    g.ks[d] = ks[d];
+    g.kin[d] = ki[d];
+    g.kout[d] = ko[d];
+  }
+  const int sms = sm_count();
+  pl.tiles_per_row = cdiv(g.L, Tile<In, Acc>::kTile);
+  if ((g.sa == 1 || g.L == 1) && (g.so == 1 || g.L == 1)) {
+    bool vec_ok = std::is_same<In, Acc>::value && (((uintptr_t)r.a & 15) == 0) && (((uintptr_t)r.out & 15) == 0);
+    for (int d = 0; d < K && vec_ok; ++d)
+      if ((ki[d] * (int64_t)sizeof(In)) % 16 || (ko[d] * (int64_t)sizeof(Acc)) % 16) vec_ok = false;
+    pl.vec_ok = vec_ok;
+    pl.kind = (g.M >= 2 * sms || pl.tiles_per_row <= 1) ? 0 : 1;
+  } else {
+    pl.vec_ok = 0;
+    pl.kind = 2;
+  }
+  return pl;
+}
+
+template <class Acc>
+size_t lookback_bytes(int64_t ntiles) {
+  return 16 + (size_t)((ntiles * 4 + 15) / 16) * 16 + (size_t)ntiles * 2 * sizeof(Acc);
+}
+
+template <class In, class Acc>
+int scan_typed(const ScanReq& r, cudaStream_t s, size_t* need_only) {
+  ScanPlan pl = scan_plan<In, Acc>(r);
+  const ScanDev& g = pl.g;
+  if (g.K > kMaxCollapsed) return fail(MPB_ERR_SHAPE, "cumsum: too many dims after collapsing");
+  const size_t need = pl.kind == 1 ? lookback_bytes<Acc>(g.M * pl.tiles_per_row) : 0;
+  if (need_only) {
+    *need_only = need;
+    return MPB_OK;
+  }
+  if (g.M * g.L == 0) return MPB_OK;
+  const In* a = static_cast<const In*>(r.a);
+  Acc* out = static_cast<Acc*>(r.out);
+  const int sms = sm_count();
+  switch (pl.kind) {
+    case 0: {
+      int64_t blocks = g.M < (int64_t)sms * 64 ? g.M : (int64_t)sms * 64;
+      k_scan_rows<In, Acc><<<(unsigned)blocks, kScanThreads, 0, s>>>(a, out, g, pl.vec_ok);
+      return launch_check("cumsum_rows");
+    }
+    case 1: {
+      if (r.scratch_bytes < need || !r.scratch)
+        return fail(MPB_ERR_SCRATCH, "cumsum: scratch of %zu bytes needed, %zu given", need, r.scratch_bytes);
+      int rc = cuda_check(cudaMemsetAsync(r.scratch, 0, need, s), "cumsum scratch clear");
+      if (rc) return rc;
+      const int64_t ntiles = g.M * pl.tiles_per_row;
+      k_scan_lookback<In, Acc><<<(unsigned)ntiles, kScanThreads, 0, s>>>(a, out, g, pl.vec_ok,
+                                                                       static_cast<char*>(r.scratch),
+                                                                       pl.tiles_per_row);
+      return launch_check("cumsum_lookback");
+    }
+    default: {
+      int64_t blocks = cdiv(g.M, kScanThreads);
+      if (blocks > (int64_t)sms * 64) blocks = (int64_t)sms * 64;
+      if (blocks < 1) blocks = 1;
+      k_scan_cols<In, Acc><<<(unsigned)blocks, kScanThreads, 0, s>>>(a, out, g);
+      return launch_check("cumsum_cols");
+    }
+  }
+}
+
+template <class Acc>
+int scan_in(const ScanReq& r, cudaStream_t s, size_t* need) {
+  switch (r.in_dt) {
+    case MPB_BOOL: return scan_typed<boolean, Acc>(r, s, need);
+    case MPB_I8: return scan_typed<int8_t, Acc>(r, s, need);
+    case MPB_I16: return scan_typed<int16_t, Acc>(r, s, need);
+    case MPB_I32: return scan_typed<int32_t, Acc>(r, s, need);
+    case MPB_I64: return scan_typed<int64_t, Acc>(r, s, need);
+    case MPB_U8: return scan_typed<uint8_t, Acc>(r, s, need);
+    case MPB_U16: return scan_typed<uint16_t, Acc>(r, s, need);
+    case MPB_U32: return scan_typed<uint32_t, Acc>(r, s, need);
+    case MPB_U64: return scan_typed<uint64_t, Acc>(r, s, need);
+    default: return fail(MPB_ERR_DTYPE, "cumsum: input dtype %d not supported", r.in_dt);
+  }
+}
+
+int scan_dispatch(const ScanReq& r, cudaStream_t s, size_t* need) {
+  if (r.ndim < 1 || r.ndim > MPB_MAX_DIMS || r.axis < 0 || r.axis >= r.ndim)
+    return fail(MPB_ERR_INVALID, "cumsum: bad ndim/axis (%d, %d)", r.ndim, r.axis);
+  switch (r.out_dt) {
+    case MPB_F32:
+      if (r.in_dt == MPB_F32) return scan_typed<float, float>(r, s, need);
+      break;
+    case MPB_F64:
+      if (r.in_dt == MPB_F64) return scan_typed<double, double>(r, s, need);
+      break;
+    case MPB_I64: return scan_in<int64_t>(r, s, need);
+    default: break;
+  }
+  return fail(MPB_ERR_DTYPE, "cumsum: input dtype %d -> output dtype %d not supported", r.in_dt, r.out_dt);
+}
+
+}  // namespace
+
+size_t scan_scratch_bytes(const ScanReq& r) {
+  size_t need = 0;
+  if (scan_dispatch(r, nullptr, &need) != MPB_OK) return 0;
+  return need;
+}
+
+int scan_run(const ScanReq& r, cudaStream_t s) {
+  if (!r.a || !r.out) {
+    int64_t n = 1;
+    for (int i = 0; i < r.ndim; ++i) n *= r.shape[i];
+    if (n == 0) return MPB_OK;
+    return fail(MPB_ERR_INVALID, "cumsum: null pointer");
+  }
+  return scan_dispatch(r, s, nullptr);
+}
+
+}  // namespace mpb

@@ -1,0 +1,166 @@
+"""Axis-0 sharding across the GPUs of one node (one process per GPU).
+
+musapy is single-device (docs/adr/ADR.md:896-906); this module is the new
+multi-GPU path. A ``ShardedArray`` holds this rank's contiguous block of rows
+of a global array; broadcast operands (a row vector) are replicated.
+
+* elementwise ops run on each shard independently (no communication);
+* reductions over non-leading axes stay local;
+* full reductions reduce the local shard on the GPU, move one tiny record per
+  rank with ONE collective over NVLink (NCCL all_reduce for sum/mean, NCCL
+  all_gather of (value, index) records for argmax/argmin), and finish on the
+  device with a one-thread combine kernel, so no host round trip is needed.
+
+The process group is torch.distributed's (backend "nccl" on GPUs, "gloo" in
+the CPU tests of the combine logic).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import dtypes as _dt
+from . import errors, ops
+from ._lib import LIB, RED_OPS, check, i64arr
+from .array import Array, empty
+
+
+def shard_rows(n_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) rows of `rank`: contiguous blocks, the first n % world
+    ranks one row larger."""
+    base, extra = divmod(n_rows, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class ShardedArray:
+    """This rank's rows [row0, row0 + local.shape[0]) of a global array."""
+
+    def __init__(self, local: Array, global_shape: tuple, row0: int, group=None) -> None:
+        self.local = local
+        self.global_shape = tuple(global_shape)
+        self.row0 = int(row0)
+        self.group = group
+
+    @property
+    def dtype(self) -> _dt.Dtype:
+        return self.local.dtype
+
+    @property
+    def global_size(self) -> int:
+        n = 1
+        for s in self.global_shape:
+            n *= s
+        return n
+
+
+def _world(group) -> tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(group), dist.get_rank(group)
+    return 1, 0
+
+
+def add(x: ShardedArray, row: Array, out: Array | None = None) -> ShardedArray:
+    """Broadcast add of a replicated operand; local, no communication."""
+    return ShardedArray(ops.add(x.local, row, out=out), x.global_shape, x.row0, x.group)
+
+
+def sum_axis(x: ShardedArray, axis: int, out: Array | None = None) -> ShardedArray:
+    """Reduction over a non-leading axis: local per shard."""
+    if axis % len(x.global_shape) == 0:
+        raise errors.ShapeError("sum over the sharded axis needs a collective: use sum_all")
+    return ShardedArray(ops.sum(x.local, axis=axis, out=out), x.global_shape[:axis] + x.global_shape[axis + 1:],
+                        x.row0, x.group)
+
+
+class _SumCombine:
+    """Scratch of a full sum/mean: the local partial and the combined value."""
+
+    def __init__(self, dev: int, out_dt: _dt.Dtype) -> None:
+        self.partial = torch.empty(1, dtype=torch.float64, device=f"cuda:{dev}")
+        self.sum_out = empty((), out_dt, dev)
+        self.mean_out = empty((), out_dt, dev)
+
+
+def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array, Array]:
+    """Global sum and mean of a float array: local f32/f64 sum written as f64,
+    one all_reduce of 8 bytes, mean over the true global element count."""
+    a = x.local
+    if a.dtype.code not in (_dt.F32, _dt.F64):
+        raise errors.DtypeError("sum_all: float32/float64 shards only")
+    dev = a._dev
+    c = combine or _SumCombine(dev, a.dtype)
+    cd = a.dtype
+    mask = (1 << a.ndim) - 1
+    shape_c, strides_c = i64arr(a.shape), i64arr(a.strides)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    nbytes = LIB.mpb_reduce_scratch_bytes(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code,
+                                          mask, cd.code)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
+    check(LIB.mpb_reduce(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code, mask,
+                         c.partial.data_ptr(), _dt.F64, cd.code, 1,
+                         scratch.data_ptr() if scratch is not None else None, nbytes, stream), "sum_all")
+    world, _ = _world(x.group)
+    if world > 1:
+        dist.all_reduce(c.partial, op=dist.ReduceOp.SUM, group=x.group)
+    check(LIB.mpb_shard_sum_finalize(c.partial.data_ptr(), float(x.global_size), a.dtype.code,
+                                     c.sum_out.data_ptr, c.mean_out.data_ptr, stream), "sum_all")
+    return c.sum_out, c.mean_out
+
+
+class _ArgCombine:
+    def __init__(self, dev: int, world: int) -> None:
+        self.rec = torch.empty(2, dtype=torch.int64, device=f"cuda:{dev}")
+        self.all = torch.empty(2 * world, dtype=torch.int64, device=f"cuda:{dev}")
+        self.index = empty((), _dt.int64, dev)
+        self.value = torch.empty(1, dtype=torch.float64, device=f"cuda:{dev}")
+
+
+def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | None = None) -> Array:
+    """Global argmax/argmin (flat index, first occurrence, musapy's NaN rule):
+    local (value, index) record, one all_gather of 16 bytes per rank, device
+    combine in rank order."""
+    a = x.local
+    dev = a._dev
+    world, rank = _world(x.group)
+    c = combine or _ArgCombine(dev, world)
+    src = a if a.dtype.code in (_dt.F32, _dt.F64, _dt.F16, _dt.BF16, _dt.I64, _dt.U64) else ops.astype(a, _dt.int64)
+    mask = (1 << src.ndim) - 1
+    shape_c, strides_c = i64arr(src.shape), i64arr(src.strides)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    op = RED_OPS["argmax_rec" if is_max else "argmin_rec"]
+    nbytes = LIB.mpb_reduce_scratch_bytes(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
+                                          src.dtype.code)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
+    # only the shard holding global element 0 applies the first-element NaN rule
+    check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
+                         c.rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
+                         scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
+    if world > 1:
+        dist.all_gather_into_tensor(c.all, c.rec, group=x.group)
+        recs = c.all
+        row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
+        starts = [shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)]
+    else:
+        recs = c.rec
+        starts = [0]
+    is_int = 1 if src.dtype.code in (_dt.I64, _dt.U64) else 0
+    check(LIB.mpb_shard_arg_combine(recs.data_ptr(), world, i64arr(starts), 1 if is_max else 0, is_int,
+                                    c.index.data_ptr, c.value.data_ptr(), stream), "argreduce_all")
+    return c.index
+
+
+def combine_records_host(recs: np.ndarray, starts, is_max: bool, is_int: bool) -> int:
+    """Host restatement of the device combine (k_arg_combine), used by the
+    CPU tests of the sharded logic: recs is int64 [world, 2]."""
+    best_i, best_v, have = 0, None, False
+    for r, (vb, li) in enumerate(recs.tolist()):
+        if li == np.iinfo(np.int64).max:
+            continue
+        v = vb if is_int else float(np.array([vb], np.int64).view(np.float64)[0])
+        if not is_int and r == 0 and li == 0 and v != v:
+            return 0
+        if not have or (v > best_v if is_max else v < best_v):
+            best_v, best_i, have = v, li + starts[r], True
+    return best_i if have else 0

@@ -1,0 +1,105 @@
+"""The parity oracle (and the C++ host logic) against the reference's own
+known answers (tests/golden/reference_kats.py). CPU only."""
+import numpy as np
+import pytest
+
+from tests.golden import reference_kats as K
+from tests.golden_util import check_values, host, long_name
+
+
+@pytest.mark.parametrize("case", K.BINARY, ids=lambda c: c[0])
+def test_binary(oracle, case):
+    src, op, a, b, exp, kw = case
+    ad, bd = kw.get("a_dtype", "f32"), kw.get("b_dtype", "f32")
+    x, y = host(a, ad, oracle), host(b, bd, oracle)
+    # The reference tests run on the CPU device: JAX promotion (all_gpu=False).
+    got = oracle.binary(op, x, y)
+    if "out_dtype" in kw:
+        assert oracle.NAMES[oracle.code_of(got.dtype)] == long_name(kw["out_dtype"]), src
+    check_values(got, exp, kw.get("tol"), src)
+
+
+@pytest.mark.parametrize("case", K.UNARY, ids=lambda c: c[0] + c[1])
+def test_unary(oracle, case):
+    src, op, a, exp, kw = case
+    got = oracle.unary(op, host(a, kw.get("dtype", "f32"), oracle))
+    check_values(got, exp, kw.get("tol"), src)
+
+
+@pytest.mark.parametrize("case", K.CLAMP, ids=lambda c: c[0])
+def test_clamp(oracle, case):
+    src, a, lo, hi, exp, kw = case
+    check_values(oracle.clamp(host(a, kw.get("dtype", "f32"), oracle), lo, hi), exp, None, src)
+
+
+@pytest.mark.parametrize("case", K.COMPARE, ids=lambda c: c[0] + c[1])
+def test_compare(oracle, case):
+    src, op, a, b, exp, kw = case
+    got = oracle.compare(op, host(a, kw.get("a_dtype", "f32"), oracle), host(b, kw.get("b_dtype", "f32"), oracle))
+    assert got.tolist() == exp, src
+
+
+@pytest.mark.parametrize("case", K.CAST, ids=lambda c: c[0])
+def test_cast(oracle, case):
+    src, a, sd, dd, exp = case
+    got = oracle.cast(host(a, sd, oracle), oracle.NAMES.index(long_name(dd)))
+    check_values(got, exp, None, src)
+
+
+@pytest.mark.parametrize("case", K.REDUCE, ids=lambda c: c[0] + c[1])
+def test_reduce(oracle, case):
+    src, op, a, axis, keep, exp, kw = case
+    got = oracle.reduce(op, host(a, kw.get("dtype", "f32"), oracle), axis, keep)
+    if "out_dtype" in kw:
+        assert oracle.NAMES[oracle.code_of(got.dtype)] == long_name(kw["out_dtype"]), src
+    check_values(np.asarray(got), exp, kw.get("tol"), src)
+
+
+@pytest.mark.parametrize("case", K.CUMSUM, ids=lambda c: c[0])
+def test_cumsum(oracle, case):
+    src, a, axis, exp, kw = case
+    got = oracle.cumsum(host(a, kw.get("dtype", "f32"), oracle), axis)
+    check_values(got, exp, kw.get("tol"), src)
+
+
+@pytest.mark.parametrize("case", K.PROMOTE, ids=lambda c: f"{c[0]}+{c[1]}:{c[2]}")
+def test_promote_oracle_and_library(oracle, case):
+    a, b, gpu, want, line = case
+    ca, cb = oracle.NAMES.index(a), oracle.NAMES.index(b)
+    assert oracle.NAMES[oracle.promote(ca, cb, gpu)] == want, f"{K.PROMOTE_SRC}:{line}"
+    from musapy_b200._lib import LIB
+
+    assert oracle.NAMES[LIB.mpb_promote(ca, cb, 1 if gpu else 0)] == want, f"{K.PROMOTE_SRC}:{line}"
+
+
+def test_promote_exhaustive_agreement(oracle):
+    """The C++ restatement and the oracle's agree on all 15x15x2 pairs."""
+    from musapy_b200._lib import LIB
+
+    for a in range(15):
+        for b in range(15):
+            for g in (0, 1):
+                assert LIB.mpb_promote(a, b, g) == oracle.promote(a, b, bool(g)), (a, b, g)
+
+
+@pytest.mark.parametrize("case", K.BROADCAST_SHAPE, ids=lambda c: str(c[3]))
+def test_broadcast_shape(case):
+    from musapy_b200._lib import LIB, i64arr
+
+    a, b, want, line = case
+    out = i64arr([0] * 8)
+    n = LIB.mpb_broadcast_shape(len(a), i64arr(a), len(b), i64arr(b), out)
+    if want is None:
+        assert n < 0, f"{K.BROADCAST_SRC}:{line}"
+    else:
+        assert list(out[:n]) == want, f"{K.BROADCAST_SRC}:{line}"
+
+
+@pytest.mark.parametrize("case", K.BROADCAST_STRIDES, ids=lambda c: str(c[4]))
+def test_broadcast_strides(case):
+    from musapy_b200._lib import LIB, i64arr
+
+    shape, strides, target, want, line = case
+    out = i64arr([0] * max(1, len(target)))
+    LIB.mpb_broadcast_strides(len(shape), i64arr(shape), i64arr(strides), len(target), i64arr(target), out)
+    assert list(out[: len(target)]) == want, f"{K.BROADCAST_SRC}:{line}"

@@ -1,0 +1,408 @@
+"""GPU parity: the CUDA engine against the oracle (the reference CPU path
+restated in oracle/oracle.c) on the same seeded inputs.
+
+Bars (the north-star parity contract):
+  * bit-exact: integer / bool / comparison / argmax / argmin / cast / max /
+    min / IEEE add-sub-mul-div / complex arithmetic;
+  * <= 2 ulp: sin / cos / exp / log / pow;
+  * sums, means, cumsums: |gpu - cpu| <= rtol * sum|x| with rtol 1e-5 (f32)
+    or 1e-12 (f64).
+"""
+import zlib
+
+import numpy as np
+import pytest
+
+from tests.helpers import assert_bits_equal, assert_sum_close, assert_ulp
+
+pytestmark = pytest.mark.gpu
+
+RTOL = {np.dtype(np.float32): 1e-5, np.dtype(np.float64): 1e-12}
+
+
+def dev(ms, x):
+    return ms.from_numpy(np.asarray(x), device="cuda:0")
+
+
+def rand(rng, shape, dtype):
+    dtype = np.dtype(dtype)
+    if dtype.kind == "f":
+        return rng.standard_normal(shape).astype(dtype)
+    if dtype.kind == "c":
+        return (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)).astype(dtype)
+    if dtype == np.bool_:
+        return rng.random(shape) < 0.5
+    info = np.iinfo(dtype)
+    return rng.integers(max(info.min, -1000), min(info.max, 1000), size=shape).astype(dtype)
+
+
+# ------------------------------------------------------------- config 1
+def test_config1_broadcast_add_and_row_sum(ms, oracle):
+    """f32 (4096,1) + (4096,) from seed 0, then sum(axis=1)."""
+    rng = np.random.default_rng(0)
+    a = rng.random((4096, 1), dtype=np.float32) * 2 - 1
+    b = rng.random(4096, dtype=np.float32) * 2 - 1
+    c = ms.add(dev(ms, a), dev(ms, b))
+    want = oracle.binary("add", a, b)
+    assert_bits_equal(c.numpy(), want, "config1 add")
+    s = ms.sum(c, axis=1).numpy()
+    assert_sum_close(s, oracle.reduce("sum", want, axis=1), np.abs(want).sum(axis=1), 1e-5, "config1 sum")
+
+
+# ------------------------------------------------------ binary arithmetic
+VIEWS = ["contig", "bcast_row", "bcast_col", "scalar", "transposed", "flipped", "offset_slice", "strided"]
+
+
+def make_operands(rng, view, dtype):
+    if view == "contig":
+        return rand(rng, (37, 129), dtype), rand(rng, (37, 129), dtype)
+    if view == "bcast_row":
+        return rand(rng, (64, 256), dtype), rand(rng, (256,), dtype)
+    if view == "bcast_col":
+        return rand(rng, (64, 1), dtype), rand(rng, (64, 256), dtype)
+    if view == "scalar":
+        return rand(rng, (), dtype), rand(rng, (5, 7, 9), dtype)
+    if view == "transposed":
+        return rand(rng, (96, 80), dtype).T, rand(rng, (80, 96), dtype)
+    if view == "flipped":
+        return rand(rng, (33, 65), dtype)[::-1, ::-1], rand(rng, (33, 65), dtype)
+    if view == "offset_slice":
+        return rand(rng, (1001,), dtype)[1:1001], rand(rng, (1000,), dtype)
+    return rand(rng, (40, 60, 8), dtype)[::2, 1::3, :], rand(rng, (20, 20, 8), dtype)[:, ::-1]
+
+
+def to_dev_view(ms, x):
+    """Device array with the same strides/offset as a numpy view."""
+    base = x
+    while base.base is not None and isinstance(base.base, np.ndarray):
+        base = base.base
+    if x.size == 0 or x.flags.c_contiguous:
+        return dev(ms, x)
+    # rebuild through the device: copy the base, then take an equivalent view
+    bd = dev(ms, base)
+    off = (x.__array_interface__["data"][0] - base.__array_interface__["data"][0]) // x.itemsize
+    from musapy_b200.array import _view
+
+    return _view(bd, x.shape, [s // x.itemsize for s in x.strides], off)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
+@pytest.mark.parametrize("view", VIEWS)
+def test_binary_bit_exact(ms, oracle, dtype, op, view):
+    rng = np.random.default_rng(zlib.crc32(f"{op}/{view}".encode()))
+    a, b = make_operands(rng, view, dtype)
+    got = getattr(ms, op)(to_dev_view(ms, a), to_dev_view(ms, b)).numpy()
+    assert_bits_equal(got, oracle.binary(op, a, b), f"{op} {view}")
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_pow_ulp(ms, oracle, dtype):
+    rng = np.random.default_rng(3)
+    a = (0.1 + 3.9 * rng.random(100_000)).astype(dtype)
+    b = (-2 + 4 * rng.random(100_000)).astype(dtype)
+    got = ms.pow(dev(ms, a), dev(ms, b)).numpy()
+    assert_ulp(got, oracle.binary("pow", a, b), 2, "pow")
+
+
+def test_binary_special_values(ms, oracle):
+    v = np.array([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, np.nan, 1e-45, 3.4e38, -3.4e38], np.float32)
+    a, b = np.meshgrid(v, v)
+    for op in ["add", "sub", "mul", "div"]:
+        got = getattr(ms, op)(dev(ms, a), dev(ms, b)).numpy()
+        assert_bits_equal(got, oracle.binary(op, a, b), op)
+    assert_ulp(ms.pow(dev(ms, np.abs(a)), dev(ms, b)).numpy(), oracle.binary("pow", np.abs(a), b), 2, "pow special")
+
+
+def test_mixed_dtype_transposed_promotion(ms, oracle):
+    """Config 2 (small): int64 A^T + float64 row -> float64 (fused cast)."""
+    rng = np.random.default_rng(2)
+    A = rng.integers(-1000, 1001, (512, 384)).astype(np.int64)
+    row = rng.standard_normal(512)
+    got = ms.add(ms.transpose(dev(ms, A)), dev(ms, row))
+    assert got.dtype == ms.float64
+    assert_bits_equal(got.numpy(), oracle.binary("add", A.T, row), "i64^T + f64")
+
+
+def test_gpu_narrow_promotion(ms, oracle):
+    """On the device musapy promotes f32+f64 to the narrower f32 (dtype.rs:302-338)."""
+    rng = np.random.default_rng(4)
+    a = rng.standard_normal(1000).astype(np.float32)
+    b = rng.standard_normal(1000)
+    got = ms.add(dev(ms, a), dev(ms, b))
+    assert got.dtype == ms.float32
+    assert_bits_equal(got.numpy(), oracle.binary("add", a, b, all_gpu=True), "f32 + f64 on device")
+
+
+# --------------------------------------------------------------- complex
+@pytest.mark.parametrize("dtype", [np.complex64, np.complex128])
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
+def test_complex_bit_exact(ms, oracle, dtype, op):
+    rng = np.random.default_rng(5)
+    a, b = rand(rng, (3000,), dtype), rand(rng, (3000,), dtype)
+    got = getattr(ms, op)(dev(ms, a), dev(ms, b)).numpy()
+    assert_bits_equal(got, oracle.binary(op, a, b), f"{op} {dtype}")
+
+
+@pytest.mark.parametrize("dtype", [np.complex64, np.complex128])
+def test_complex_unary_and_compare(ms, oracle, dtype):
+    rng = np.random.default_rng(6)
+    a = rand(rng, (2000,), dtype)
+    b = a.copy()
+    b[::3] += 1
+    assert_bits_equal(ms.neg(dev(ms, a)).numpy(), oracle.unary("neg", a), "neg")
+    assert_bits_equal(ms.abs(dev(ms, a)).numpy(), oracle.unary("abs", a), "abs")
+    assert_bits_equal(ms.eq(dev(ms, a), dev(ms, b)).numpy(), oracle.compare("eq", a, b), "eq")
+    assert_bits_equal(ms.ne(dev(ms, a), dev(ms, b)).numpy(), oracle.compare("ne", a, b), "ne")
+
+
+# ----------------------------------------------------------------- unary
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("op", ["sin", "cos", "exp", "log"])
+def test_transcendental_ulp(ms, oracle, dtype, op):
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal(200_000).astype(dtype) * 10
+    if op == "log":
+        x = np.abs(x) + np.asarray(1e-30, dtype)
+    if op == "exp":
+        x = x * 8
+    got = getattr(ms, op)(dev(ms, x)).numpy()
+    assert_ulp(got, oracle.unary(op, x), 2, op)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("op", ["abs", "sign", "neg"])
+def test_simple_unary_exact(ms, oracle, dtype, op):
+    x = np.array([0.0, -0.0, 1.5, -2.5, np.inf, -np.inf, np.nan, 1e-300 if dtype == np.float64 else 1e-40], dtype)
+    x = np.concatenate([x, np.random.default_rng(8).standard_normal(1000).astype(dtype)])
+    assert_bits_equal(getattr(ms, op)(dev(ms, x)).numpy(), oracle.unary(op, x), op)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_clamp_exact(ms, oracle, dtype):
+    x = np.concatenate([np.array([np.nan, -np.inf, np.inf, -0.0, 0.5, -0.5], dtype),
+                        np.random.default_rng(9).standard_normal(5000).astype(dtype)])
+    got = ms.clamp(dev(ms, x), -0.5, 0.5).numpy()
+    assert_bits_equal(got, oracle.clamp(x, -0.5, 0.5), "clamp")
+
+
+def test_config2_chain_small(ms, oracle):
+    """Config 2 chain exp(sin(x)) -> clamp(-0.5, 0.5) on N(0,1) f32, per call."""
+    x = np.random.default_rng(2).standard_normal(1 << 18, dtype=np.float32)
+    s = ms.sin(dev(ms, x))
+    s_want = oracle.unary("sin", x)
+    assert_ulp(s.numpy(), s_want, 2, "sin")
+    e = ms.exp(s)
+    e_want = oracle.unary("exp", s.numpy())
+    assert_ulp(e.numpy(), e_want, 2, "exp")
+    c = ms.clamp(e, -0.5, 0.5)
+    assert_bits_equal(c.numpy(), oracle.clamp(e.numpy(), -0.5, 0.5), "clamp")
+
+
+# ----------------------------------------------------------- comparisons
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.float16, np.int64, np.int32])
+@pytest.mark.parametrize("op", ["eq", "ne", "lt", "gt", "le", "ge"])
+def test_compare_exact(ms, oracle, dtype, op):
+    rng = np.random.default_rng(10)
+    a = rand(rng, (300, 20), dtype)
+    b = a.copy()
+    b[::2] = rand(rng, b[::2].shape, dtype)
+    if np.dtype(dtype).kind == "f":
+        a[0, :4] = [np.nan, 0.0, -0.0, np.inf]
+        b[0, :4] = [np.nan, -0.0, 0.0, np.inf]
+    got = getattr(ms, op)(dev(ms, a), dev(ms, b))
+    assert got.dtype == ms.bool_
+    assert_bits_equal(got.numpy(), oracle.compare(op, a, b), op)
+    # broadcast against a row
+    got = getattr(ms, op)(dev(ms, a), dev(ms, b[0])).numpy()
+    assert_bits_equal(got, oracle.compare(op, a, b[0]), op + " bcast")
+
+
+# ------------------------------------------------------------------ casts
+CASTS = [("float32", "bfloat16"), ("bfloat16", "float32"), ("float32", "float16"), ("float16", "float32"),
+         ("float64", "float32"), ("float32", "float64"), ("int64", "float64"), ("int64", "float32"),
+         ("float64", "int64"), ("float32", "int64"), ("int32", "float32"), ("uint64", "float32"),
+         ("float64", "float16"), ("float64", "bfloat16"), ("int8", "float64"), ("float32", "int8"),
+         ("float32", "uint8"), ("float32", "bool"), ("complex64", "complex128"), ("float32", "complex64"),
+         ("float64", "complex128"), ("uint8", "int64"), ("int64", "int16")]
+
+
+@pytest.mark.parametrize("src,dst", CASTS)
+def test_cast_exact(ms, oracle, src, dst):
+    rng = np.random.default_rng(11)
+    sd = oracle.np_of(oracle.NAMES.index(src))
+    if sd.kind == "f" or src == "bfloat16":
+        x = (rng.standard_normal(20000) * np.exp(rng.uniform(-20, 20, 20000)))
+        x = np.concatenate([x, [0.0, -0.0, np.inf, -np.inf, np.nan, 1e30, -1e30, 127.9, -128.9, 255.5, 3e9]])
+        x = oracle.cast(x.astype(np.float64), oracle.NAMES.index(src))
+    elif sd.kind == "c":
+        x = rand(rng, (5000,), sd)
+    else:
+        info = np.iinfo(sd)
+        x = rng.integers(info.min, info.max, size=20000, dtype=sd, endpoint=True)
+    d = ms.from_numpy(x, device="cuda:0")
+    got = d.astype(dst).numpy()
+    want = oracle.cast(x, oracle.NAMES.index(dst))
+    assert_bits_equal(got, want, f"{src}->{dst}")
+
+
+def test_cast_strided_transposed(ms, oracle):
+    x = np.random.default_rng(12).standard_normal((300, 500)).astype(np.float32)
+    got = ms.transpose(dev(ms, x)).astype("bf16").numpy()
+    want = oracle.cast(np.ascontiguousarray(x.T), oracle.BF16)
+    assert_bits_equal(got, want, "transposed cast")
+    assert_bits_equal(ms.contiguous(ms.transpose(dev(ms, x))).numpy(), np.ascontiguousarray(x.T), "contiguous")
+
+
+# ------------------------------------------------------------ reductions
+RED_SHAPES = [((256, 256), 0), ((256, 256), 1), ((100, 17), 1), ((1025, 5), 0), ((1025, 5), 1),
+              ((7, 1024), 1), ((5000, 3), 0), ((3, 70000), 1), ((1_000_000,), None), ((2, 3, 4), (0, 2)),
+              ((6, 50, 40), (1, 2)), ((6, 50, 40), (0, 1)), ((16, 33, 65), -1), ((4, 5, 6, 7), (0, 3))]
+
+
+@pytest.mark.parametrize("shape,axis", RED_SHAPES)
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_reduce_float(ms, oracle, shape, axis, dtype):
+    rng = np.random.default_rng(13)
+    x = rng.standard_normal(shape).astype(dtype)
+    xd = dev(ms, x)
+    ax_abs = oracle.reduce("sum", np.abs(x).astype(np.float64), axis)
+    for op in ["sum", "mean"]:
+        got = getattr(ms, op)(xd, axis=axis).numpy()
+        want = oracle.reduce(op, x, axis)
+        truth = oracle.reduce(op, x.astype(np.float64), axis)
+        L = x.size // max(1, want.size)
+        bound = ax_abs / (L if op == "mean" else 1)
+        assert_sum_close(got, want, bound, RTOL[np.dtype(dtype)], op, truth=truth)
+    for op in ["max", "min", "argmax", "argmin"]:
+        got = getattr(ms, op)(xd, axis=axis).numpy()
+        assert_bits_equal(got, oracle.reduce(op, x, axis), f"{op} {shape} {axis}")
+
+
+def test_reduce_prod_and_keepdims(ms, oracle):
+    rng = np.random.default_rng(14)
+    x = (0.5 + rng.random((64, 48))).astype(np.float32)
+    # products of <= 64 factors stay well inside the f32 range
+    for axis, v in [(0, x), (1, x), (None, x[:4, :10])]:
+        got = ms.prod(dev(ms, v), axis=axis).numpy()
+        want = oracle.reduce("prod", v, axis)
+        np.testing.assert_allclose(got, want, rtol=1e-5)
+    for op in ["sum", "max", "argmax", "mean"]:
+        for axis in [0, 1, (0, 1)]:
+            got = getattr(ms, op)(dev(ms, x), axis=axis, keepdims=True)
+            want = oracle.reduce(op, x, axis, keepdims=True)
+            assert got.shape == want.shape, (op, axis)
+
+
+def test_reduce_nan_ties_signed_zero(ms, oracle):
+    """First occurrence on ties, NaN only when it is the first element,
+    +0/-0 resolved by position - bit-identical to the sequential CPU loop."""
+    cases = [
+        [np.nan, 1.0, 5.0, 5.0],
+        [1.0, np.nan, 5.0, 5.0, 2.0],
+        [-0.0, 0.0, -1.0],
+        [0.0, -0.0, -1.0],
+        [np.nan, np.nan],
+        [-np.inf, -np.inf],
+        [3.0, 3.0, 3.0],
+    ]
+    for c in cases:
+        for dtype in (np.float32, np.float64):
+            x = np.array(c, dtype)
+            for op in ["max", "min", "argmax", "argmin"]:
+                assert_bits_equal(getattr(ms, op)(dev(ms, x)).numpy(), oracle.reduce(op, x, None), f"{op} {c}")
+    # long rows (split / block kernels) with a NaN first and ties spread out
+    x = np.zeros(1 << 20, np.float32)
+    x[[5, 70000, 900000]] = 7.0
+    for op in ["max", "argmax", "argmin", "min"]:
+        assert_bits_equal(getattr(ms, op)(dev(ms, x)).numpy(), oracle.reduce(op, x, None), op + " long")
+    x[0] = np.nan
+    for op in ["max", "argmax"]:
+        assert_bits_equal(getattr(ms, op)(dev(ms, x)).numpy(), oracle.reduce(op, x, None), op + " nan-first")
+    m = np.random.default_rng(15).standard_normal((300, 700)).astype(np.float32)
+    m[:, 0] = np.nan
+    m[5, 3] = np.nan
+    for axis in (0, 1):
+        for op in ["max", "argmax", "min", "argmin"]:
+            assert_bits_equal(getattr(ms, op)(dev(ms, m), axis=axis).numpy(), oracle.reduce(op, m, axis), f"{op} {axis}")
+
+
+@pytest.mark.parametrize("dtype", [np.int64, np.int32, np.int8, np.uint8, np.bool_])
+def test_reduce_int_exact(ms, oracle, dtype):
+    rng = np.random.default_rng(16)
+    x = rand(rng, (256, 256), dtype)
+    for op in ["sum", "prod", "max", "min", "argmax", "argmin"]:
+        for axis in [None, 0, 1]:
+            got = getattr(ms, op)(dev(ms, x), axis=axis).numpy()
+            assert_bits_equal(got, oracle.reduce(op, x, axis), f"{op} {axis}")
+    got = ms.mean(dev(ms, x), axis=1)
+    assert got.dtype == ms.float64
+    assert_sum_close(got.numpy(), oracle.reduce("mean", x, 1), np.abs(x.astype(np.float64)).sum(1) / 256, 1e-12)
+
+
+@pytest.mark.parametrize("dtype", [np.complex64, np.complex128])
+def test_reduce_complex(ms, oracle, dtype):
+    rng = np.random.default_rng(17)
+    x = rand(rng, (30, 40), dtype)
+    for op in ["sum", "mean", "prod"]:
+        for axis in [None, 0, 1]:
+            got = getattr(ms, op)(dev(ms, x), axis=axis).numpy()
+            want = oracle.reduce(op, x, axis)
+            np.testing.assert_allclose(got, want, rtol=1e-4 if dtype == np.complex64 else 1e-10)
+
+
+def test_reduce_strided_views(ms, oracle):
+    rng = np.random.default_rng(12)
+    base = rng.random((64, 64), dtype=np.float32)
+    v = base[:, ::-1]
+    d = ms.flip(dev(ms, base), axis=1)
+    t = ms.transpose(dev(ms, base))
+    for op in ["max", "min", "argmax", "argmin"]:
+        for axis in (0, 1, None):
+            assert_bits_equal(getattr(ms, op)(d, axis=axis).numpy(), oracle.reduce(op, v, axis), f"flip {op}")
+            assert_bits_equal(getattr(ms, op)(t, axis=axis).numpy(), oracle.reduce(op, base.T, axis), f"T {op}")
+    for axis in (0, 1, None):
+        assert_sum_close(ms.sum(d, axis=axis).numpy(), oracle.reduce("sum", v, axis),
+                         oracle.reduce("sum", np.abs(v).astype(np.float64), axis), 1e-5)
+
+
+# ---------------------------------------------------------------- cumsum
+CUMSUM_CASES = [((4,), 0), ((2, 2), None), ((2, 2), 0), ((2, 2), 1), ((3, 70000), 1), ((1300,), 0), ((1537,), 0),
+                ((100_000,), 0), ((262, 4096), 1), ((64, 33, 5), 1), ((5000, 7), 0), ((1 << 21,), None),
+                ((400, 4097), -1)]
+
+
+@pytest.mark.parametrize("shape,axis", CUMSUM_CASES)
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.int64, np.int32])
+def test_cumsum(ms, oracle, shape, axis, dtype):
+    rng = np.random.default_rng(18)
+    x = rand(rng, shape, dtype) if np.dtype(dtype).kind == "i" else rng.random(shape).astype(dtype)
+    ms.ops.set_scan_status_check(True)
+    got = ms.cumsum(dev(ms, x), axis=axis).numpy()
+    ms.ops.set_scan_status_check(False)
+    want = oracle.cumsum(x, axis)
+    if np.dtype(dtype).kind == "i":
+        assert_bits_equal(got, want, "cumsum int")
+    else:
+        absx = oracle.cumsum(np.abs(x).astype(np.float64), axis)
+        truth = oracle.cumsum(x.astype(np.float64), axis)
+        assert_sum_close(got, want, absx, RTOL[np.dtype(dtype)], "cumsum", truth=truth)
+
+
+def test_cumsum_ones_boundaries(ms, oracle):
+    """test_reduction.py:321-351: 65,536 / 65,537 / 1M ones in int64."""
+    for n in (65536, 65537, 1_000_000):
+        r = ms.cumsum(ms.ones(n, dtype="i64", device="cuda:0"), axis=0)
+        assert ms.sum(r).item() == n * (n + 1) // 2
+        assert r.numpy()[-1] == n
+
+
+# ------------------------------------------------------------ edge cases
+def test_empty_and_scalar(ms, oracle):
+    e = dev(ms, np.zeros((0, 5), np.float32))
+    assert ms.add(e, e).shape == (0, 5)
+    assert ms.sum(e, axis=0).numpy().tolist() == [0.0] * 5
+    assert ms.sum(e, axis=1).shape == (0,)
+    s = dev(ms, np.array(3.0, np.float32))
+    assert ms.add(s, s).item() == 6.0
+    assert ms.cumsum(e).shape == (0,)
