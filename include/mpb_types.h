@@ -1,4 +1,5 @@
-// Shared enums and limits of the musapy-b200 engine (host + device).
+// Shared enums and limits of the musapy-b200 engine (host, device and the
+// public C-ABI in musapy_b200.h).
 //
 // The dtype numbering follows the declaration order of musapy's `Dtype`
 // enum (rust/musapy-core/src/dtype.rs:25-41) so that a tag crossing the

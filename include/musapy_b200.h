@@ -1,0 +1,165 @@
+/*
+ * libmusapy_b200 - musapy's stride-aware elementwise and reduction engine
+ * for NVIDIA B200 (sm_100a). Public C-ABI.
+ *
+ * Two families of entry points:
+ *
+ *  1. Extended entry points (mpb_*): one call per musapy operator, a dtype tag
+ *     per operand (promotion casts are fused into the kernels), an int status
+ *     return, caller-owned scratch. These are what the Python surface
+ *     (musapy_b200) binds, and what a host layer in any language should bind.
+ *     They replace the per-dtype kernel wrappers that musapy's operator layer
+ *     calls from rust/musapy-ops/src/op_builder.rs (launch_binary! ...
+ *     launch_argreduce_partial!, :38-223, and the cast/cumsum dispatch at
+ *     :968-1045 and :3321-3330).
+ *
+ *  2. Reference-named kernel symbols (musapy_<op>_<dtype>_v2 / _v3), declared
+ *     in include/musapy_kernels_v2.h: the exact set and signatures of
+ *     rust/musapy-ops/src/kernels.rs:16-343, so a CUDA build of musapy's Rust
+ *     layers can link this library unchanged.
+ *
+ * Conventions (shared with musapy's kernel contract, docs/adr/ADR.md:322-338):
+ *  - strides and offsets are in ELEMENTS and may be 0 (broadcast) or negative
+ *    (flipped views); each data pointer addresses the logical element
+ *    [0, ..., 0] of its view (the view offset is already applied);
+ *  - outputs are C-contiguous;
+ *  - shape / stride arrays are host memory read during the call only;
+ *  - every launch is asynchronous on `stream`; the library never allocates
+ *    device memory (scratch is passed in) and never synchronises, except
+ *    mpb_cumsum_status which reads a status word back;
+ *  - dtype tags follow musapy's Dtype enum order
+ *    (rust/musapy-core/src/dtype.rs:25-41), see enum mpb_dtype.
+ */
+#ifndef MUSAPY_B200_H
+#define MUSAPY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "mpb_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without requiring the CUDA headers. */
+typedef struct CUstream_st* mpb_stream_t;
+
+/* ---------------------------------------------------------------- status */
+
+/* Message describing the last non-OK status returned on this thread. */
+const char* mpb_last_error(void);
+/* ABI version of this header (bumped on incompatible changes). */
+int mpb_version(void);
+/* Multiprocessor count of the current device (148 on B200; 148 without a device). */
+int mpb_num_sms(void);
+/* Number of kernels this library has launched in the process so far. */
+unsigned long long mpb_launch_count(void);
+
+/* ------------------------------------------------------- host-side helpers */
+
+/* Result dtype of a binary op: rust/musapy-core/src/dtype.rs:302-338
+ * (`promote`); all_gpu=1 selects the narrow-first rule musapy applies when
+ * every input lives on the device. Returns -1 when no promotion exists. */
+int mpb_promote(int a_dtype, int b_dtype, int all_gpu);
+
+/* NumPy broadcast of two shapes: rust/musapy-ops/src/broadcast.rs:24-58
+ * (`broadcast_shape`). Writes max(na, nb) extents to `out`; returns that
+ * ndim, or -1 when the shapes are incompatible. */
+int mpb_broadcast_shape(int na, const int64_t* a_shape, int nb, const int64_t* b_shape, int64_t* out);
+
+/* Strides of an operand against a broadcast target:
+ * rust/musapy-ops/src/broadcast.rs:71-92 (`broadcast_strides`). */
+void mpb_broadcast_strides(int ndim, const int64_t* shape, const int64_t* strides, int target_ndim,
+                           const int64_t* target, int64_t* out);
+
+/* The engine's dimension collapsing (replaces the per-element offset_nd of
+ * kernels/include/common.h:42-51): drops extent-1 dims and merges adjacent
+ * dims that every operand allows. `strides` holds nops x ndim values;
+ * writes the collapsed shape and nops x result strides; returns the
+ * collapsed ndim (>= 1), or -1 on bad arguments. Host only. */
+int mpb_collapse(int ndim, const int64_t* shape, int nops, const int64_t* strides, int64_t* out_shape,
+                 int64_t* out_strides);
+
+/* Kernel class the reduction planner picks (1 row_warp, 2 row_block,
+ * 3 row_split, 4 col, 5 col_split, 6 gen; 0 empty) and the output count M,
+ * reduced length L and split count. Host only; negative status on error. */
+int mpb_reduce_plan(int ndim, const int64_t* shape, const int64_t* strides, int in_dtype, uint64_t axes_mask,
+                    int64_t* M, int64_t* L, int64_t* splits);
+
+/* ------------------------------------------------------------ elementwise */
+
+/* out = op(a[, b]) over `shape`, for every mpb_ew_op:
+ *   MPB_ADD..MPB_POW   binary arithmetic; replaces musapy_{add,sub,mul,div,pow}
+ *                      _{f32,f64,c64,c128}_v2 (rust/musapy-ops/src/kernels.rs:19-28,
+ *                      :102-109) plus the cast temporaries of op_builder.rs:410-417
+ *   MPB_EQ..MPB_GE     comparisons, out_dtype MPB_BOOL (kernels.rs:84-95, :114-117)
+ *   MPB_SIN..MPB_NEG   unary math (kernels.rs:31-44, :110-113)
+ *   MPB_CLAMP          p0 = lo, p1 = hi (kernels.rs:47-48)
+ *   MPB_CAST           dtype conversion / strided copy (kernels.rs:51-81, :119-124)
+ *   MPB_FILL           out = p0 (+ i*p1 for complex); a and b unused
+ * a_strides / b_strides are already broadcast to `shape` (0 on broadcast
+ * dims); b is NULL for unary ops. compute_dtype is the promoted dtype the op
+ * is evaluated in; a and b are read in their own dtypes and converted in
+ * registers. */
+int mpb_elementwise(int op, int ndim, const int64_t* shape, const void* a, int a_dtype, const int64_t* a_strides,
+                    const void* b, int b_dtype, const int64_t* b_strides, void* out, int out_dtype,
+                    int compute_dtype, double p0, double p1, mpb_stream_t stream);
+
+/* -------------------------------------------------------------- reductions */
+
+/* Device scratch (bytes) mpb_reduce needs for this request; 0 when none. */
+size_t mpb_reduce_scratch_bytes(int op, int ndim, const int64_t* shape, const int64_t* strides, const void* a,
+                                int in_dtype, uint64_t axes_mask, int compute_dtype);
+
+/* Reduce the dims set in axes_mask (bit d = dim d) with an mpb_red_op.
+ * Replaces the naive / small_axis / partial / mid / final kernel families of
+ * kernels.rs:139-180, :222-304 and the host path choice of
+ * op_builder.rs:2310-3139 with one call. The output is C-contiguous over the
+ * kept dims in order. nan_first_rule=1 applies musapy's CPU rule for
+ * max/min/argmax/argmin (a NaN is the answer only when it is the first
+ * element). Multiple axes reduce in one pass; argmax/argmin over several axes
+ * report the flat index over those axes (reduction.rs:186-223). Integer
+ * inputs narrower than 64 bits must be widened to int64 by the caller (as
+ * musapy's cast_array does); MPB_R_ARGMAX_REC / _ARGMIN_REC write a 16-byte
+ * {value bits, index} record per output for cross-shard combining. */
+int mpb_reduce(int op, int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype,
+               uint64_t axes_mask, void* out, int out_dtype, int compute_dtype, int nan_first_rule, void* scratch,
+               size_t scratch_bytes, mpb_stream_t stream);
+
+/* ------------------------------------------------------------------ cumsum */
+
+/* Device scratch (bytes) mpb_cumsum needs; 0 when none. */
+size_t mpb_cumsum_scratch_bytes(int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype,
+                                int axis, void* out, int out_dtype);
+
+/* Inclusive prefix sum along `axis`; out_dtype is the compute dtype (f32,
+ * f64, or i64 for integer inputs). Replaces musapy_cumsum_{i64,f32,f64}_v3
+ * (kernels.rs:185-187) without its 256^3 length limit. The scratch is
+ * cleared by the call itself. */
+int mpb_cumsum(int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype, int axis,
+               void* out, int out_dtype, void* scratch, size_t scratch_bytes, mpb_stream_t stream);
+
+/* Synchronises `stream` and reads the status word a look-back cumsum left in
+ * its scratch: MPB_OK, or MPB_ERR_TIMEOUT when a bounded wait gave up. */
+int mpb_cumsum_status(const void* scratch, mpb_stream_t stream);
+
+/* ---------------------------------------------------- axis-0 sharding (new) */
+
+/* Device combine of per-rank argmax/argmin records (MPB_R_ARG*_REC output,
+ * all-gathered in rank order) into one global flat index; rank_offsets[r] is
+ * the flat index of rank r's first element. No counterpart in musapy, which
+ * has no multi-GPU path. */
+int mpb_shard_arg_combine(const int64_t* records, int nranks, const int64_t* rank_offsets, int is_max, int is_int,
+                          int64_t* out_index, double* out_value, mpb_stream_t stream);
+
+/* Writes sum and mean (true global count) of an all-reduced f64 total in the
+ * array dtype (MPB_F32 or MPB_F64). No counterpart in musapy. */
+int mpb_shard_sum_finalize(const double* total, double count, int out_dtype, void* sum_out, void* mean_out,
+                           mpb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUSAPY_B200_H */

@@ -20,6 +20,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 BUILD = os.path.join(HERE, "_build")
 LIBDIR = os.path.join(HERE, "_lib")
 LIBNAME = "libmusapy_b200.so"
@@ -37,6 +38,8 @@ NVCC_FLAGS = ARCH + [
     "shared",
     "-I",
     CSRC,
+    "-I",
+    INCLUDE,
 ]
 
 
@@ -52,7 +55,8 @@ def lib_path() -> str:
 
 
 def _headers() -> list[str]:
-    return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+    return (glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+            + glob.glob(os.path.join(INCLUDE, "*.h")))
 
 
 def _stale(src: str, obj: str, newest_header: float) -> bool:

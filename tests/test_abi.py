@@ -1,0 +1,52 @@
+"""The C-ABI library loads on a machine without a GPU and exports every
+function the public headers declare (no compute calls here)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(ROOT, "include", h) for h in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if h.endswith(".h")]
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        for m in re.finditer(r"\b((?:mpb|musapy)_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_headers_declare_entry_points():
+    names = declared_functions()
+    assert "mpb_elementwise" in names and "mpb_reduce" in names and "mpb_cumsum" in names
+
+
+def test_library_exports_every_declared_symbol():
+    from musapy_b200._lib import LIB_PATH
+
+    lib = ctypes.CDLL(LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing[:20]}"
+
+
+def test_library_has_no_undefined_cuda_symbols_beyond_runtime():
+    from musapy_b200._lib import LIB_PATH
+
+    out = subprocess.run(["nm", "-D", "--undefined-only", LIB_PATH], capture_output=True, text=True).stdout
+    undefined = [l.split()[-1] for l in out.splitlines() if l.strip()]
+    forbidden = [u for u in undefined if "MemcpyBatch" in u or "Memcpy3DBatch" in u]
+    assert not forbidden
+
+
+def test_version_and_promote_without_gpu():
+    from musapy_b200._lib import LIB
+
+    assert LIB.mpb_version() >= 1
+    assert LIB.mpb_promote(4, 11, 0) == 11  # int64 + float64 -> float64
