@@ -127,6 +127,23 @@ int mpb_reduce(int op, int ndim, const int64_t* shape, const int64_t* strides, c
                uint64_t axes_mask, void* out, int out_dtype, int compute_dtype, int nan_first_rule, void* scratch,
                size_t scratch_bytes, mpb_stream_t stream);
 
+/* Same as mpb_reduce but with no scratch argument: the scratch comes from an
+ * array built into the library (256 KiB per GPU, held from the library's
+ * load on that GPU until the process exits). No counterpart in musapy. It
+ * exists for callers that cannot allocate device memory: an application that
+ * embeds this library and owns the whole device budget through its own pool,
+ * or a latency-critical loop in which cudaMalloc / cudaFree must not run
+ * because they can synchronise the device. It allocates nothing. Requests
+ * whose plan needs more than 256 KiB of scratch return MPB_ERR_SCRATCH (use
+ * mpb_reduce for those). All calls on a GPU share the array and it keeps the
+ * last call's contents (nothing in it needs to start at zero), so calls that
+ * can overlap on the GPU race: order them on one stream or with events. The
+ * first call on each device looks up the array's device address with that
+ * device current; make that first call before any stream capture begins. */
+int mpb_reduce_noalloc(int op, int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype,
+                       uint64_t axes_mask, void* out, int out_dtype, int compute_dtype, int nan_first_rule,
+                       mpb_stream_t stream);
+
 /* ------------------------------------------------------------------ cumsum */
 
 /* Device scratch (bytes) mpb_cumsum needs; 0 when none. */
