@@ -27,10 +27,13 @@ int cuda_check(cudaError_t e, const char* what) {
 }
 
 static unsigned long long g_launches = 0;
+static thread_local bool g_preserve_last_error = false;
+
+void set_preserve_last_error(bool on) { g_preserve_last_error = on; }
 
 int launch_check(const char* what) {
   __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED);
-  return cuda_check(cudaGetLastError(), what);
+  return cuda_check(g_preserve_last_error ? cudaPeekAtLastError() : cudaGetLastError(), what);
 }
 
 int sm_count() {

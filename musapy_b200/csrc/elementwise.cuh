@@ -5,11 +5,11 @@
 // kernels/elementwise.mu:35-573. Instead of one thread per element with a
 // 64-bit div/mod per dim per operand (offset_nd, common.h:42-51), the host
 // collapses dims and classifies the call:
-//   EW_CONTIG  1-D streams: 16-byte vector loads/stores, 2 packs in flight
+//   EW_CONTIG  1-D streams: 16-byte vector loads/stores, 4 packs in flight
 //              per thread, grid-stride over a grid sized to the SM count;
 //   EW_ROWS    [outer..., inner] with every operand unit-stride or broadcast
-//              along `inner`: the same vector packs, one magic-number
-//              division per pack to find the row;
+//              along `inner`: the same vector packs, work items of one row
+//              chunk so the row index math runs once per 1024 packs;
 //   EW_TILED   an input whose unit stride lies on an outer dim (a transposed
 //              view): 32x32 tiles staged through shared memory so that both
 //              the read and the write are coalesced, cast fused on the way in;
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kEwThreads) k_ew_contig(Op op, const TA* __res
                                                           int64_t n, int a_bc, int b_bc) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
   constexpr int N = 16 / min_size3<TA, TBv, TO>();
-  constexpr int UNR = 2;
+  constexpr int UNR = 4;
   const int64_t nvec = n / N;
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
@@ -140,87 +140,79 @@ struct NdArgs {
 
 // --------------------------------------------------------------- EW_ROWS
 // Rows of `inner` elements (inner % N == 0); operand inner stride is 0 or 1
-// (flag bits a_bc/b_bc); row r starts at sum(coord_d * s[d]) over the outer
-// dims. All unit-stride row starts are 16-byte aligned (host-checked).
-template <class Op, class TC, class TA, class TB, class TO, int NIN, class IdxT>
+// (a_bc/b_bc flag the broadcast ones); row r starts at sum(coord_d * s[d])
+// over the outer dims, every unit-stride row start 16-byte aligned
+// (host-checked). Work items are (row, chunk of kRowChunk packs): the row and
+// its offsets are computed once per item, then each thread moves kRowUnr
+// lane-strided packs (coalesced 16-byte accesses) with all loads in flight
+// before the first store.
+constexpr int kRowUnr = 4;
+constexpr int kRowChunk = kEwThreads * kRowUnr;  // packs per work item
+
+template <class Op, class TC, class TA, class TB, class TO, int NIN>
 __global__ void __launch_bounds__(kEwThreads) k_ew_rows(Op op, const TA* __restrict__ a,
                                                         const TB* __restrict__ b, TO* __restrict__ out,
-                                                        NdArgs g, IdxT nslots, FastDiv slots_div,
+                                                        NdArgs g, int64_t nitems, int64_t cpr, FastDiv cpr_div,
                                                         int a_bc, int b_bc) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
   constexpr int N = 16 / min_size3<TA, TBv, TO>();
-  constexpr int UNR = 2;
-  const IdxT slots_per_row = (IdxT)(g.shape[g.ndim - 1] / N);
-  const IdxT gtid = (IdxT)blockIdx.x * blockDim.x + threadIdx.x;
-  const IdxT gstride = (IdxT)gridDim.x * blockDim.x;
-  for (IdxT s = gtid; s < nslots; s += gstride * UNR) {
-    VPack<TA, N> pa[UNR];
-    VPack<TBv, N> pb[UNR];
-    TA as[UNR];
-    TBv bs[UNR];
-    IdxT orow[UNR], ocol[UNR];
+  const int64_t inner = g.shape[g.ndim - 1];
+  const int64_t spr = inner / N;  // packs per row
+  for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x) {
+    int64_t row, chunk;
+    if (nitems < 0xffffffffLL) {
+      uint32_t q, r;
+      cpr_div.divmod((uint32_t)item, q, r);
+      row = q;
+      chunk = r;
+    } else {
+      row = item / cpr;
+      chunk = item - row * cpr;
+    }
+    int64_t oa = 0, ob = 0, rr = row;
+    for (int d = g.ndim - 2; d > 0; --d) {
+      const int64_t c = rr % g.shape[d];
+      rr /= g.shape[d];
+      oa += c * g.sa[d];
+      ob += c * g.sb[d];
+    }
+    oa += rr * g.sa[0];
+    ob += rr * g.sb[0];
+    const TA* ar = a + oa;
+    const TBv* br = reinterpret_cast<const TBv*>(b) + ob;
+    TO* orow = out + row * inner;
+    const int64_t p0 = chunk * kRowChunk + threadIdx.x;
+    VPack<TA, N> pa[kRowUnr];
+    VPack<TBv, N> pb[kRowUnr];
+    TA as = TA{};
+    TBv bs = TBv{};
+    if (a_bc) as = ar[0];
+    if constexpr (NIN == 2) {
+      if (b_bc) bs = br[0];
+    }
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const IdxT si = s + (IdxT)u * gstride;
-      if (si < nslots) {
-        IdxT row, cs;
-        if constexpr (sizeof(IdxT) == 4) {
-          uint32_t q, r;
-          slots_div.divmod((uint32_t)si, q, r);
-          row = q;
-          cs = r;
-        } else {
-          row = si / slots_per_row;
-          cs = si - row * slots_per_row;
-        }
-        orow[u] = row;
-        ocol[u] = cs * N;
-        int64_t oa = 0, ob = 0;
-        IdxT rr = row;
-        for (int d = g.ndim - 2; d >= 0; --d) {
-          IdxT q, c;
-          if constexpr (sizeof(IdxT) == 4) {
-            uint32_t qq, cc;
-            g.fd[d].divmod((uint32_t)rr, qq, cc);
-            q = qq;
-            c = cc;
-          } else {
-            q = rr / (IdxT)g.shape[d];
-            c = rr - q * (IdxT)g.shape[d];
-          }
-          oa += (int64_t)c * g.sa[d];
-          ob += (int64_t)c * g.sb[d];
-          rr = q;
-        }
-        if (a_bc) {
-          as[u] = a[oa];
-        } else {
-          vload<TA, N, true>(pa[u], a + oa + (int64_t)cs * N);
-        }
+    for (int u = 0; u < kRowUnr; ++u) {
+      const int64_t p = p0 + u * kEwThreads;
+      if (p < spr) {
+        if (!a_bc) vload<TA, N, true>(pa[u], ar + p * N);
         if constexpr (NIN == 2) {
-          const TBv* bb = reinterpret_cast<const TBv*>(b);
-          if (b_bc) {
-            bs[u] = bb[ob];
-          } else {
-            vload<TBv, N, false>(pb[u], bb + ob + (int64_t)cs * N);
-          }
+          if (!b_bc) vload<TBv, N, false>(pb[u], br + p * N);
         }
       }
     }
-    const int64_t inner = g.shape[g.ndim - 1];
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const IdxT si = s + (IdxT)u * gstride;
-      if (si < nslots) {
+    for (int u = 0; u < kRowUnr; ++u) {
+      const int64_t p = p0 + u * kEwThreads;
+      if (p < spr) {
         VPack<TO, N> po;
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          const TA av = a_bc ? as[u] : pa[u][j];
+          const TA av = a_bc ? as : pa[u][j];
           TBv bv{};
-          if constexpr (NIN == 2) bv = b_bc ? bs[u] : pb[u][j];
+          if constexpr (NIN == 2) bv = b_bc ? bs : pb[u][j];
           po[j] = Apply<Op, TC, TO, NIN>::run(op, av, bv);
         }
-        vstore<TO, N>(out + (int64_t)orow[u] * inner + ocol[u], po);
+        vstore<TO, N>(orow + p * N, po);
       }
     }
   }

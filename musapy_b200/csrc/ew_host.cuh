@@ -81,7 +81,7 @@ Plan make_plan(const EwReq& r) {
       }
     }
     (void)oo;
-    if (ok && (g.numel / N) > 0 && (g.numel / N) < 0xffffffffLL) {
+    if (ok && (g.numel / N) > 0) {
       pl.kind = EW_ROWS;
       return pl;
     }
@@ -158,16 +158,21 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
   switch (pl.kind) {
     case EW_CONTIG: {
       const int64_t nvec = g.numel / N;
-      k_ew_contig<Op, TC, TA, TB, TO, NIN><<<grid_for(nvec, kEwThreads * 2), kEwThreads, 0, s>>>(
+      k_ew_contig<Op, TC, TA, TB, TO, NIN><<<grid_for(nvec, kEwThreads * 4), kEwThreads, 0, s>>>(
           op, a, b, out, g.numel, pl.a_bc, pl.b_bc);
       return launch_check("ew_contig");
     }
     case EW_ROWS: {
       NdArgs na = nd_args(g, NIN);
-      const int64_t nslots = g.numel / N;
       const int64_t spr = g.shape[g.ndim - 1] / N;
-      k_ew_rows<Op, TC, TA, TB, TO, NIN, uint32_t><<<grid_for(nslots, kEwThreads * 2), kEwThreads, 0, s>>>(
-          op, a, b, out, na, (uint32_t)nslots, FastDiv((uint32_t)spr), pl.a_bc, pl.b_bc);
+      const int64_t rows = g.numel / g.shape[g.ndim - 1];
+      const int64_t cpr = cdiv(spr, kRowChunk);
+      const int64_t nitems = rows * cpr;
+      int64_t blocks = nitems;
+      const int64_t cap = (int64_t)sm_count() * 16;
+      if (blocks > cap) blocks = cap;
+      k_ew_rows<Op, TC, TA, TB, TO, NIN><<<(unsigned)(blocks < 1 ? 1 : blocks), kEwThreads, 0, s>>>(
+          op, a, b, out, na, nitems, cpr, FastDiv((uint32_t)(cpr < 0xffffffffLL ? cpr : 1)), pl.a_bc, pl.b_bc);
       return launch_check("ew_rows");
     }
     case EW_TILED: {

@@ -10,8 +10,12 @@ namespace mpb {
 int fail(int code, const char* fmt, ...);
 // MPB_OK when `e` is cudaSuccess, otherwise records the CUDA error.
 int cuda_check(cudaError_t e, const char* what);
-// Checks cudaGetLastError() after a launch.
+// Checks the CUDA error state after a launch: cleared (cudaGetLastError) for
+// the extended API, which reports it as a status; left in place
+// (cudaPeekAtLastError) while a reference-ABI wrapper runs, so the caller's own
+// cudaGetLastError() still sees it as with musapy's kernels.
 int launch_check(const char* what);
+void set_preserve_last_error(bool on);
 // Multiprocessor count of the current device (cached per device).
 int sm_count();
 

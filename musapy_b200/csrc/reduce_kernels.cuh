@@ -99,6 +99,23 @@ struct PArg {
     if (better(v, idx, a)) a = Acc{v, idx};
   }
   MPB_D static Acc merge(const Acc& l, const Acc& r) { return better(r.v, r.i, l) ? r : l; }
+  // NaN-ignoring extreme of two values (fmax/fmin return the non-NaN one).
+  MPB_D static V pick(V a, V b) {
+    if constexpr (std::is_same<V, int64_t>::value) {
+      return IS_MAX ? (a > b ? a : b) : (a < b ? a : b);
+    } else if constexpr (std::is_same<V, float>::value) {
+      return IS_MAX ? fmaxf(a, b) : fminf(a, b);
+    } else {
+      return IS_MAX ? fmax(a, b) : fmin(a, b);
+    }
+  }
+  // Can a group whose extreme is m and whose smallest index is `first` change
+  // the accumulator? Any element that `better` would take makes this true:
+  // a strictly better value implies m is strictly better, and an equal value
+  // only wins with an index below a.i, which needs first < a.i.
+  MPB_D static bool improves(V m, const Acc& a, int64_t first) {
+    return IS_MAX ? (m > a.v || (m == a.v && first < a.i)) : (m < a.v || (m == a.v && first < a.i));
+  }
 };
 
 template <class P>
@@ -253,11 +270,32 @@ MPB_D void fold_segment_vec(typename P::Acc& acc, const typename P::In* __restri
       for (int k = 0; k < (int)((VEC * sizeof(In) + 15) / 16); ++k)
         w[u][k] = ld_stream16(reinterpret_cast<const char*>(p + c + u * step) + 16 * k);
     }
+    if constexpr (P::kArg) {
+      // Extreme of the UNR*VEC values first (one min/max per element); the
+      // exact in-order (value, index) rule runs only when it can matter.
+      auto m = P::pick(cvt<decltype(acc.v)>(reinterpret_cast<const In*>(w[0])[0]),
+                       cvt<decltype(acc.v)>(reinterpret_cast<const In*>(w[0])[VEC > 1 ? 1 : 0]));
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const In* v = reinterpret_cast<const In*>(w[u]);
+      for (int u = 0; u < UNR; ++u) {
+        const In* v = reinterpret_cast<const In*>(w[u]);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) P::fold(acc, v[j], lbase + (c + u * step + j) * rwi);
+        for (int j = 0; j < VEC; ++j) m = P::pick(m, cvt<decltype(acc.v)>(v[j]));
+      }
+      if (P::improves(m, acc, lbase + c * rwi)) {
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+          const In* v = reinterpret_cast<const In*>(w[u]);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) P::fold(acc, v[j], lbase + (c + u * step + j) * rwi);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const In* v = reinterpret_cast<const In*>(w[u]);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) P::fold(acc, v[j], lbase + (c + u * step + j) * rwi);
+      }
     }
   }
   for (; c < li; c += step) {
