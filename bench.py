@@ -378,6 +378,131 @@ def run_b200(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- per-config suite
+def config_inputs(name: str):
+    """Seeded inputs of BASELINE configs 1-4 (numpy PCG64; seeds 0, 2, 1, 4)."""
+    import numpy as np
+
+    if name == "C1":
+        rng = np.random.default_rng(0)
+        a = rng.random((4096, 1), dtype=np.float32) * 2 - 1
+        b = rng.random(4096, dtype=np.float32) * 2 - 1
+        return {"a": a, "b": b}
+    if name == "C2":
+        rng = np.random.default_rng(2)
+        A = rng.integers(-1000, 1001, (8192, 8192), dtype=np.int64)
+        row = rng.standard_normal(8192)
+        x = rng.standard_normal(1 << 28, dtype=np.float32)
+        return {"A": A, "row": row, "x": x}
+    if name == "C3":
+        rng = np.random.default_rng(1)
+        return {"x": rng.standard_normal((64, 4096, 4096), dtype=np.float32)}
+    if name == "C4":
+        rng = np.random.default_rng(4)
+        x = rng.standard_normal(1 << 30, dtype=np.float32)
+        a = (0.1 + 3.9 * rng.random(1 << 30, dtype=np.float32)).astype(np.float16)
+        b = (-2 + 4 * rng.random(1 << 30, dtype=np.float32)).astype(np.float16)
+        re, im = rng.standard_normal((2, 1 << 27), dtype=np.float32)
+        re2, im2 = rng.standard_normal((2, 1 << 27), dtype=np.float32)
+        return {"x": x, "a": a, "b": b, "z1": (re + 1j * im).astype(np.complex64),
+                "z2": (re2 + 1j * im2).astype(np.complex64)}
+    raise KeyError(name)
+
+
+def run_suite(args) -> None:
+    import gc
+
+    import torch
+
+    import musapy_b200 as ms
+
+    peak, peak_kind = measured_peak()
+    stream = torch.cuda.current_stream()
+
+    def timeit(fn, nbytes, iters=None):
+        iters = iters or args.steps
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = ms._lib.launch_count()
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_per = e0.elapsed_time(e1) / iters
+        return ms_per, nbytes / (ms_per * 1e-3) / 1e9, (ms._lib.launch_count() - n0) // iters
+
+    def emit(cfg, op, nbytes, fn, note=""):
+        t, gbs, launches = timeit(fn, nbytes)
+        print(json.dumps({"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4), "bytes": int(nbytes), "launches": launches,
+                          "peak": peak, "peak_kind": peak_kind, "note": note}), flush=True)
+
+    cfgs = args.suite.split(",")
+    if "C1" in cfgs:
+        d = config_inputs("C1")
+        a, b = ms.from_numpy(d["a"]), ms.from_numpy(d["b"])
+        c = ms.add(a, b)
+        r = ms.sum(c, axis=1)
+        emit("C1", "add (4096,1)+(4096,)", 4096 * 4 * 2 + 4096 * 4096 * 4, lambda: ms.add(a, b, out=c))
+        emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r))
+    if "C2" in cfgs:
+        d = config_inputs("C2")
+        A, row, x = ms.from_numpy(d["A"]), ms.from_numpy(d["row"]), ms.from_numpy(d["x"])
+        del d
+        At = ms.transpose(A)
+        o = ms.add(At, row)
+        emit("C2", "add i64^T (8192,8192) + f64 row -> f64", 8192 * 8192 * 8 * 2 + 8192 * 8,
+             lambda: ms.add(At, row, out=o))
+        s = ms.sin(x)
+        e = ms.exp(s)
+        cl = ms.clamp(e, -0.5, 0.5)
+        n = 1 << 28
+        emit("C2", "sin f32 2^28", n * 8, lambda: ms.sin(x, out=s))
+        emit("C2", "exp f32 2^28", n * 8, lambda: ms.exp(s, out=e))
+        emit("C2", "clamp f32 2^28", n * 8, lambda: ms.clamp(e, -0.5, 0.5, out=cl))
+        del A, At, o, s, e, cl, x, row
+    if "C3" in cfgs:
+        x = ms.from_numpy(config_inputs("C3")["x"])
+        n = 64 * 4096 * 4096 * 4
+        for axis, oelems in [(2, 64 * 4096), (0, 4096 * 4096), ((0, 2), 4096)]:
+            for op in ("sum", "max", "mean"):
+                out = getattr(ms, op)(x, axis=axis)
+                f = (lambda op=op, axis=axis: getattr(ms, op)(x, axis=axis)) if isinstance(axis, tuple) else \
+                    (lambda op=op, axis=axis, out=out: getattr(ms, op)(x, axis=axis, out=out))
+                emit("C3", f"{op} axis={axis}", n + oelems * 4, f)
+        am = ms.argmax(x, axis=1)
+        emit("C3", "argmax axis=1", n + 64 * 4096 * 8, lambda: ms.argmax(x, axis=1, out=am))
+        cs = ms.cumsum(x, axis=-1)
+        emit("C3", "cumsum axis=-1", 2 * n, lambda: ms.cumsum(x, axis=-1, out=cs))
+        del x, cs, am
+    if "C4" in cfgs:
+        d = config_inputs("C4")
+        n = 1 << 30
+        x = ms.from_numpy(d["x"])
+        xb = x.astype("bf16")
+        back = xb.astype("f32")
+        emit("C4", "astype f32->bf16 2^30", n * 6, lambda: ms.astype(x, "bf16", out=xb))
+        emit("C4", "astype bf16->f32 2^30", n * 6, lambda: ms.astype(xb, "f32", out=back))
+        del x, xb, back
+        a, b = ms.from_numpy(d["a"]), ms.from_numpy(d["b"])
+        p = ms.pow(a, b)
+        emit("C4", "pow f16 2^30", n * 6, lambda: ms.pow(a, b, out=p))
+        del p
+        lt = ms.lt(a, b)
+        emit("C4", "lt f16 -> bool 2^30", n * 5, lambda: ms.lt(a, b, out=lt))
+        emit("C4", "eq f16 -> bool 2^30", n * 5, lambda: ms.eq(a, b, out=lt))
+        del a, b, lt
+        z1, z2 = ms.from_numpy(d["z1"]), ms.from_numpy(d["z2"])
+        z = ms.mul(z1, z2)
+        emit("C4", "mul c64 2^27", (1 << 27) * 24, lambda: ms.mul(z1, z2, out=z))
+        del z1, z2, z, d
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -388,7 +513,11 @@ def main() -> None:
     ap.add_argument("--sample-rows", type=int, default=2048, help="rows of the CPU sample")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--suite", default="", help="comma list of C1..C4: time every op of those configs")
     args = ap.parse_args()
+    if args.suite:
+        run_suite(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -241,32 +241,4 @@ MPB_D void st_stream16(void* p, uint4 v) {
                : "memory");
 }
 
-// N elements of T packed into 16-byte words (N * sizeof(T) is a multiple of 16).
-template <class T, int N>
-struct Pack {
-  static constexpr int kBytes = N * (int)sizeof(T);
-  static constexpr int kWords = kBytes / 16;
-  union {
-    uint4 w[kWords > 0 ? kWords : 1];
-    T v[N];
-  };
-};
-
-template <class T, int N, bool STREAM>
-MPB_D void load_pack(Pack<T, N>& dst, const T* p) {
-  static_assert(Pack<T, N>::kBytes % 16 == 0, "pack must be whole 16-byte words");
-#pragma unroll
-  for (int w = 0; w < Pack<T, N>::kWords; ++w) {
-    const char* q = reinterpret_cast<const char*>(p) + 16 * w;
-    dst.w[w] = STREAM ? ld_stream16(q) : ld_nc16(q);
-  }
-}
-template <class T, int N>
-MPB_D void store_pack(T* p, const Pack<T, N>& src) {
-#pragma unroll
-  for (int w = 0; w < Pack<T, N>::kWords; ++w) {
-    st_stream16(reinterpret_cast<char*>(p) + 16 * w, src.w[w]);
-  }
-}
-
 }  // namespace mpb

@@ -28,31 +28,69 @@ namespace mpb {
 
 constexpr int kEwThreads = 256;
 
-// A pack of 16-byte words viewed as N elements of T.
+// A pack of N elements of T moved by vector accesses: 16-byte words, or one
+// narrower word (8/4/2/1 bytes) for an input narrower than the output.
+template <int BYTES> struct PackWord { using type = uint4; };
+template <> struct PackWord<8> { using type = uint2; };
+template <> struct PackWord<4> { using type = unsigned int; };
+template <> struct PackWord<2> { using type = unsigned short; };
+template <> struct PackWord<1> { using type = unsigned char; };
+
 template <class T, int N>
 struct VPack {
-  static constexpr int kWords = (N * (int)sizeof(T)) / 16;
-  static_assert((N * (int)sizeof(T)) % 16 == 0, "pack must be whole 16-byte words");
-  uint4 w[kWords];
+  static constexpr int kBytes = N * (int)sizeof(T);
+  static constexpr int kWordBytes = kBytes >= 16 ? 16 : kBytes;
+  static constexpr int kWords = kBytes / kWordBytes;
+  static_assert(kBytes % kWordBytes == 0, "pack must be whole words");
+  using W = typename PackWord<kWordBytes>::type;
+  W w[kWords];
   MPB_D T& operator[](int i) { return reinterpret_cast<T*>(w)[i]; }
   MPB_D const T& operator[](int i) const { return reinterpret_cast<const T*>(w)[i]; }
 };
 template <class T, int N, bool STREAM>
 MPB_D void vload(VPack<T, N>& d, const T* p) {
+  using P = VPack<T, N>;
 #pragma unroll
-  for (int i = 0; i < VPack<T, N>::kWords; ++i) {
-    const char* q = reinterpret_cast<const char*>(p) + 16 * i;
-    d.w[i] = STREAM ? ld_stream16(q) : ld_nc16(q);
+  for (int i = 0; i < P::kWords; ++i) {
+    const char* q = reinterpret_cast<const char*>(p) + P::kWordBytes * i;
+    if constexpr (P::kWordBytes == 16) {
+      d.w[i] = STREAM ? ld_stream16(q) : ld_nc16(q);
+    } else {
+      const typename P::W* qw = reinterpret_cast<const typename P::W*>(q);
+      d.w[i] = STREAM ? __ldcs(qw) : __ldg(qw);
+    }
   }
 }
+// Output packs are always whole 16-byte words (ew_pack below).
 template <class T, int N>
 MPB_D void vstore(T* p, const VPack<T, N>& s) {
+  static_assert(VPack<T, N>::kWordBytes == 16, "output packs are 16-byte words");
 #pragma unroll
   for (int i = 0; i < VPack<T, N>::kWords; ++i) st_stream16(reinterpret_cast<char*>(p) + 16 * i, s.w[i]);
 }
 
+// Elements per pack: one 16-byte word of output. Every thread's store is then
+// one 16-byte access, and a warp's stores cover whole 32-byte sectors; an input
+// wider than the output takes several words per pack, a narrower one a
+// narrower word (writing two words 32 bytes apart per thread instead left half
+// sectors to be merged in L2 and cost about a quarter of the bandwidth).
+template <class TA, class TB, class TO>
+constexpr int ew_pack() {
+  return 16 / (int)sizeof(TO) > 0 ? 16 / (int)sizeof(TO) : 1;
+}
+
 // Unused second operand of unary ops.
 struct NoArg {};
+
+template <class Op, class = void>
+struct IsPaired : std::false_type {};
+template <class Op>
+struct IsPaired<Op, std::void_t<decltype(Op::kPaired)>> : std::bool_constant<Op::kPaired> {};
+// Ops with much arithmetic per element (transcendentals, pow).
+template <class Op, class = void>
+struct IsHeavy : IsPaired<Op> {};
+template <class Op>
+struct IsHeavy<Op, std::void_t<decltype(Op::kHeavy)>> : std::bool_constant<Op::kHeavy> {};
 
 template <class Op, class TC, class TO, int NIN>
 struct Apply {
@@ -64,24 +102,48 @@ struct Apply {
       return cvt<TO>(op(cvt<TC>(a)));
     }
   }
+  // Unary float ops with a two-element form (packed f32x2 arithmetic).
+  static constexpr bool kPair = NIN == 1 && IsPaired<Op>::value && std::is_same<TC, float>::value;
+  template <class TA>
+  MPB_D static void run2(const Op& op, const TA& a0, const TA& a1, TO& o0, TO& o1) {
+    const float2 r = op.pair(make_float2(cvt<float>(a0), cvt<float>(a1)));
+    o0 = cvt<TO>(r.x);
+    o1 = cvt<TO>(r.y);
+  }
 };
 
-template <class A, class B, class C>
-constexpr int min_size3() {
-  int m = (int)sizeof(A);
-  if ((int)sizeof(B) < m) m = (int)sizeof(B);
-  if ((int)sizeof(C) < m) m = (int)sizeof(C);
-  return m;
+// Applies the op to one pack: pairs for ops that have a two-element form.
+template <class Op, class TC, class TO, int NIN, class TA, class TBv, int N>
+MPB_D void apply_pack(const Op& op, const VPack<TA, N>& pa, const VPack<TBv, N>& pb, bool a_bc, bool b_bc,
+                      const TA& as, const TBv& bs, VPack<TO, N>& po) {
+  using AP = Apply<Op, TC, TO, NIN>;
+  if constexpr (AP::kPair && N % 2 == 0) {
+#pragma unroll
+    for (int j = 0; j < N; j += 2) {
+      AP::run2(op, a_bc ? as : pa[j], a_bc ? as : pa[j + 1], po[j], po[j + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const TA av = a_bc ? as : pa[j];
+      TBv bv{};
+      if constexpr (NIN == 2) bv = b_bc ? bs : pb[j];
+      po[j] = AP::run(op, av, bv);
+    }
+  }
 }
 
 // ------------------------------------------------------------- EW_CONTIG
-template <class Op, class TC, class TA, class TB, class TO, int NIN>
-__global__ void __launch_bounds__(kEwThreads) k_ew_contig(Op op, const TA* __restrict__ a,
-                                                          const TB* __restrict__ b, TO* __restrict__ out,
-                                                          int64_t n, int a_bc, int b_bc) {
+// The loop is instantiated twice: without broadcast operands (the common
+// case, no per-element selects) and with them.
+template <bool BC, class Op, class TC, class TA, class TB, class TO, int NIN>
+MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restrict__ b, TO* __restrict__ out,
+                       int64_t n, int a_bc_in, int b_bc_in) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
-  constexpr int N = 16 / min_size3<TA, TBv, TO>();
+  constexpr int N = ew_pack<TA, TBv, TO>();
   constexpr int UNR = 4;
+  const bool a_bc = BC && a_bc_in;
+  const bool b_bc = BC && b_bc_in;
   const int64_t nvec = n / N;
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
@@ -108,13 +170,7 @@ __global__ void __launch_bounds__(kEwThreads) k_ew_contig(Op op, const TA* __res
       const int64_t vi = v + u * gstride;
       if (vi < nvec) {
         VPack<TO, N> po;
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          const TA av = a_bc ? a0 : pa[u][j];
-          TBv bv{};
-          if constexpr (NIN == 2) bv = b_bc ? b0 : pb[u][j];
-          po[j] = Apply<Op, TC, TO, NIN>::run(op, av, bv);
-        }
+        apply_pack<Op, TC, TO, NIN>(op, pa[u], pb[u], a_bc, b_bc, a0, b0, po);
         vstore<TO, N>(out + vi * N, po);
       }
     }
@@ -125,6 +181,31 @@ __global__ void __launch_bounds__(kEwThreads) k_ew_contig(Op op, const TA* __res
     TBv bv{};
     if constexpr (NIN == 2) bv = b_bc ? b0 : b[t];
     out[t] = Apply<Op, TC, TO, NIN>::run(op, av, bv);
+  }
+}
+
+// Blocks per SM the register allocation must allow (4 caps a thread at 64
+// registers). Left to itself the compiler unrolls the grid-stride loop into
+// 90-120 registers, 2 blocks per SM: fine for plain arithmetic (4 blocks cost
+// ~4% on f32 add), but ops with much arithmetic per element need the warps to
+// hide its latency (pow f16 +24%, sin +15%, exp +7%), and a narrow input word
+// (bf16 -> f32 loads 8 bytes per pack) needs them to keep enough bytes in
+// flight (+17%).
+template <class Op, class TA, class TB, class TO, int NIN>
+constexpr int ew_min_blocks() {
+  using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
+  constexpr int N = ew_pack<TA, TBv, TO>();
+  return (IsHeavy<Op>::value || VPack<TA, N>::kBytes < 16) ? 4 : 1;
+}
+
+template <class Op, class TC, class TA, class TB, class TO, int NIN>
+__global__ void __launch_bounds__(kEwThreads, ew_min_blocks<Op, TA, TB, TO, NIN>()) k_ew_contig(Op op, const TA* __restrict__ a,
+                                                          const TB* __restrict__ b, TO* __restrict__ out,
+                                                          int64_t n, int a_bc, int b_bc) {
+  if (a_bc || b_bc) {
+    contig_loop<true, Op, TC, TA, TB, TO, NIN>(op, a, b, out, n, a_bc, b_bc);
+  } else {
+    contig_loop<false, Op, TC, TA, TB, TO, NIN>(op, a, b, out, n, 0, 0);
   }
 }
 
@@ -141,7 +222,7 @@ struct NdArgs {
 // --------------------------------------------------------------- EW_ROWS
 // Rows of `inner` elements (inner % N == 0); operand inner stride is 0 or 1
 // (a_bc/b_bc flag the broadcast ones); row r starts at sum(coord_d * s[d])
-// over the outer dims, every unit-stride row start 16-byte aligned
+// over the outer dims, every unit-stride row start aligned to its pack
 // (host-checked). Work items are (row, chunk of kRowChunk packs): the row and
 // its offsets are computed once per item, then each thread moves kRowUnr
 // lane-strided packs (coalesced 16-byte accesses) with all loads in flight
@@ -149,13 +230,13 @@ struct NdArgs {
 constexpr int kRowUnr = 4;
 constexpr int kRowChunk = kEwThreads * kRowUnr;  // packs per work item
 
-template <class Op, class TC, class TA, class TB, class TO, int NIN>
-__global__ void __launch_bounds__(kEwThreads) k_ew_rows(Op op, const TA* __restrict__ a,
-                                                        const TB* __restrict__ b, TO* __restrict__ out,
-                                                        NdArgs g, int64_t nitems, int64_t cpr, FastDiv cpr_div,
-                                                        int a_bc, int b_bc) {
+template <bool BC, class Op, class TC, class TA, class TB, class TO, int NIN>
+MPB_D void rows_loop(const Op& op, const TA* __restrict__ a, const TB* __restrict__ b, TO* __restrict__ out,
+                     const NdArgs& g, int64_t nitems, int64_t cpr, FastDiv cpr_div, int a_bc_in, int b_bc_in) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
-  constexpr int N = 16 / min_size3<TA, TBv, TO>();
+  constexpr int N = ew_pack<TA, TBv, TO>();
+  const bool a_bc = BC && a_bc_in;
+  const bool b_bc = BC && b_bc_in;
   const int64_t inner = g.shape[g.ndim - 1];
   const int64_t spr = inner / N;  // packs per row
   for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x) {
@@ -205,16 +286,22 @@ __global__ void __launch_bounds__(kEwThreads) k_ew_rows(Op op, const TA* __restr
       const int64_t p = p0 + u * kEwThreads;
       if (p < spr) {
         VPack<TO, N> po;
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          const TA av = a_bc ? as : pa[u][j];
-          TBv bv{};
-          if constexpr (NIN == 2) bv = b_bc ? bs : pb[u][j];
-          po[j] = Apply<Op, TC, TO, NIN>::run(op, av, bv);
-        }
+        apply_pack<Op, TC, TO, NIN>(op, pa[u], pb[u], a_bc, b_bc, as, bs, po);
         vstore<TO, N>(orow + p * N, po);
       }
     }
+  }
+}
+
+template <class Op, class TC, class TA, class TB, class TO, int NIN>
+__global__ void __launch_bounds__(kEwThreads, ew_min_blocks<Op, TA, TB, TO, NIN>()) k_ew_rows(Op op, const TA* __restrict__ a,
+                                                        const TB* __restrict__ b, TO* __restrict__ out,
+                                                        NdArgs g, int64_t nitems, int64_t cpr, FastDiv cpr_div,
+                                                        int a_bc, int b_bc) {
+  if (a_bc || b_bc) {
+    rows_loop<true, Op, TC, TA, TB, TO, NIN>(op, a, b, out, g, nitems, cpr, cpr_div, a_bc, b_bc);
+  } else {
+    rows_loop<false, Op, TC, TA, TB, TO, NIN>(op, a, b, out, g, nitems, cpr, cpr_div, 0, 0);
   }
 }
 

@@ -20,6 +20,7 @@ struct Swapped {
 };
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+inline bool aligned_to(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes) == 0; }
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int grid_for(int64_t work_items, int per_block) {
   int64_t blocks = cdiv(work_items, per_block);
@@ -39,7 +40,7 @@ struct Plan {
 template <class TA, class TB, class TO, int NIN, bool ALLOW_TILED>
 Plan make_plan(const EwReq& r) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
-  constexpr int N = 16 / min_size3<TA, TBv, TO>();
+  constexpr int N = ew_pack<TA, TBv, TO>();
   Plan pl;
   int64_t out_st[MPB_MAX_DIMS];
   int64_t acc = 1;
@@ -58,9 +59,12 @@ Plan make_plan(const EwReq& r) {
   const bool b_unit_or_bc = NIN == 1 || (sb_in == 0 || sb_in == 1);
   pl.a_bc = (sa_in == 0);
   pl.b_bc = NIN == 2 && (sb_in == 0);
+  // input packs are N elements: whole 16-byte words, or one narrower word
+  const int a_align = N * (int)sizeof(TA) < 16 ? N * (int)sizeof(TA) : 16;
+  const int b_align = N * (int)sizeof(TBv) < 16 ? N * (int)sizeof(TBv) : 16;
   if (k == 1) {
-    if (a_unit_or_bc && b_unit_or_bc && aligned16(r.out) && (pl.a_bc || aligned16(r.a)) &&
-        (NIN == 1 || pl.b_bc || aligned16(r.b))) {
+    if (a_unit_or_bc && b_unit_or_bc && aligned16(r.out) && (pl.a_bc || aligned_to(r.a, a_align)) &&
+        (NIN == 1 || pl.b_bc || aligned_to(r.b, b_align))) {
       pl.kind = EW_CONTIG;
       return pl;
     }
@@ -68,16 +72,17 @@ Plan make_plan(const EwReq& r) {
     return pl;
   }
   // EW_ROWS: every input unit-stride or broadcast along the inner dim, with
-  // 16-byte aligned row starts for the unit-stride ones.
+  // pack-aligned row starts for the unit-stride ones.
   if (g.shape[k - 1] % N == 0 && a_unit_or_bc && b_unit_or_bc && aligned16(r.out)) {
     bool ok = true;
     for (int x = 0; x < NIN && ok; ++x) {
       const void* base = x == 0 ? r.a : r.b;
       const int esz = x == 0 ? (int)sizeof(TA) : (int)sizeof(TBv);
+      const int align = x == 0 ? a_align : b_align;
       if (g.st[x][k - 1] == 1) {
-        if (!aligned16(base)) ok = false;
+        if (!aligned_to(base, align)) ok = false;
         for (int d = 0; d < k - 1 && ok; ++d)
-          if (((g.st[x][d] * esz) % 16) != 0) ok = false;
+          if (((g.st[x][d] * esz) % align) != 0) ok = false;
       }
     }
     (void)oo;
@@ -147,7 +152,7 @@ inline TiledArgs tiled_args(const Geometry& g, int nin, int tx_op, int p) {
 template <class Op, class TC, class TA, class TB, class TO, int NIN, bool ALLOW_TILED = false>
 int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
-  constexpr int N = 16 / min_size3<TA, TBv, TO>();
+  constexpr int N = ew_pack<TA, TBv, TO>();
   Plan pl = make_plan<TA, TB, TO, NIN, ALLOW_TILED>(r);
   const Geometry& g = pl.g;
   if (g.numel == 0) return MPB_OK;

@@ -6,15 +6,17 @@
 //  * complex64 arithmetic is evaluated in f64 and narrowed once, exactly as
 //    cpu_binary_cplx (op_builder.rs:1689-1731) does; every f64 step uses an
 //    explicitly rounded intrinsic so no FMA contraction can change a bit;
-//  * f32 transcendentals are evaluated in f64 and rounded once, which keeps
-//    them within 1 ulp of the correctly rounded value (libm's sinf/expf/... are
-//    within 1 ulp too, so the two agree within 2 ulp);
+//  * f32 sin/cos/exp/log are within 1 ulp of the correctly rounded value
+//    (mathf.cuh); libm's sinf/expf/... are within 1 ulp too, so the two agree
+//    within 2 ulp. sin/cos/exp also take two elements at once (`pair`, packed
+//    f32x2 arithmetic) with results identical to the one-element form;
 //  * f16/bf16 arithmetic runs in f32 and rounds once (f32 carries >= 2p+2 bits
 //    of either format, so +,-,*,/ are correctly rounded);
 //  * sign(NaN) = sign(+-0) = +0 and clamp lets NaN through, as the CPU loops do
 //    (op_builder.rs:1878-1886, :2035-2043).
 #pragma once
 #include "common.cuh"
+#include "mathf.cuh"
 
 namespace mpb {
 
@@ -71,13 +73,39 @@ struct OpDiv {
 // 16-bit formats compute in f32 (tag OpPowLow) because one f32 rounding is
 // already far below their half-ulp.
 struct OpPow {
+  static constexpr bool kHeavy = true;
   MPB_D float operator()(float a, float b) const {
     return __double2float_rn(pow((double)a, (double)b));
   }
   MPB_D double operator()(double a, double b) const { return pow(a, b); }
 };
+// 16-bit pow: 2^(b log2 a) through the SFU (lg2.approx / ex2.approx) when a
+// is positive and finite, |b| < 64 and |b log2 a| < 24. The absolute error of
+// lg2.approx is about 2^-22, so t = b log2 a is off by at most 2^-16 and 2^t by
+// about 1e-5 relative, far under half an f16 ulp (2^-11): one more rounding to
+// 16 bits gives the correctly rounded value or a neighbour (checked over all
+// 2^32 f16 pairs: within 1 ulp of the correctly rounded value, and within 1 ulp
+// of pow evaluated in f32). Everything else (a <= 0, inf, NaN, large |b|,
+// results outside the f16 range) goes through powf.
 struct OpPowLow {
-  MPB_D float operator()(float a, float b) const { return powf(a, b); }
+  static constexpr bool kHeavy = true;
+  MPB_D static float lg2_approx(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+  }
+  MPB_D static float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+  }
+  MPB_D float operator()(float a, float b) const {
+    // a subnormal a (possible from bf16) is flushed to 0 by lg2.approx.ftz,
+    // which makes t infinite or NaN and sends it to powf
+    const float t = b * lg2_approx(a);
+    if (a > 0.0f && a < __int_as_float(0x7f800000) && fabsf(b) < 64.0f && fabsf(t) < 24.0f) return ex2_approx(t);
+    return powf(a, b);
+  }
 };
 
 // ------------------------------------------------------------- comparisons
@@ -107,19 +135,26 @@ struct OpNeC {
 
 // ------------------------------------------------------------------- unary
 struct OpSin {
-  MPB_D float operator()(float a) const { return __double2float_rn(sin((double)a)); }
+  static constexpr bool kPaired = true;
+  MPB_D float operator()(float a) const { return mathf::sinf_(a); }
+  MPB_D float2 pair(float2 a) const { return mathf::sincosf2_<0>(a); }
   MPB_D double operator()(double a) const { return sin(a); }
 };
 struct OpCos {
-  MPB_D float operator()(float a) const { return __double2float_rn(cos((double)a)); }
+  static constexpr bool kPaired = true;
+  MPB_D float operator()(float a) const { return mathf::cosf_(a); }
+  MPB_D float2 pair(float2 a) const { return mathf::sincosf2_<1>(a); }
   MPB_D double operator()(double a) const { return cos(a); }
 };
 struct OpExp {
-  MPB_D float operator()(float a) const { return __double2float_rn(exp((double)a)); }
+  static constexpr bool kPaired = true;
+  MPB_D float operator()(float a) const { return mathf::expf_(a); }
+  MPB_D float2 pair(float2 a) const { return mathf::expf2_(a); }
   MPB_D double operator()(double a) const { return exp(a); }
 };
 struct OpLog {
-  MPB_D float operator()(float a) const { return __double2float_rn(log((double)a)); }
+  static constexpr bool kHeavy = true;
+  MPB_D float operator()(float a) const { return mathf::logf_(a); }
   MPB_D double operator()(double a) const { return log(a); }
 };
 struct OpAbs {

@@ -227,8 +227,8 @@ int red_run(const RedReq& r, cudaStream_t s) {
     case MPB_R_SUM: ro.mode = 0; return red::run_sum(r, pl, ro, s);
     case MPB_R_MEAN: ro.mode = 1; return red::run_sum(r, pl, ro, s);
     case MPB_R_PROD: ro.mode = 0; return red::run_prod(r, pl, ro, s);
-    case MPB_R_MAX: ro.mode = 2; return red::run_arg(r, pl, ro, true, s);
-    case MPB_R_MIN: ro.mode = 2; return red::run_arg(r, pl, ro, false, s);
+    case MPB_R_MAX: ro.mode = 2; return red::run_ext(r, pl, ro, true, s);
+    case MPB_R_MIN: ro.mode = 2; return red::run_ext(r, pl, ro, false, s);
     case MPB_R_ARGMAX: ro.mode = 3; return red::run_arg(r, pl, ro, true, s);
     case MPB_R_ARGMIN: ro.mode = 3; return red::run_arg(r, pl, ro, false, s);
     case MPB_R_ARGMAX_REC: ro.mode = 4; return red::run_arg(r, pl, ro, true, s);

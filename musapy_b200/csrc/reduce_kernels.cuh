@@ -63,8 +63,10 @@ struct PSum {
   using In = TIn;
   using Acc = TAcc;
   static constexpr bool kArg = false;
+  static constexpr bool kExt = false;
   MPB_D static Acc ident() { return zero_of<Acc>(); }
   MPB_D static void fold(Acc& a, const In& x, int64_t) { a = radd(a, cvt<Acc>(x)); }
+  MPB_D static void fold_seq(Acc& a, const In& x, int64_t i) { fold(a, x, i); }
   MPB_D static Acc merge(const Acc& l, const Acc& r) { return radd(l, r); }
 };
 template <class TIn, class TAcc>
@@ -72,8 +74,10 @@ struct PProd {
   using In = TIn;
   using Acc = TAcc;
   static constexpr bool kArg = false;
+  static constexpr bool kExt = false;
   MPB_D static Acc ident() { return one_of<Acc>(); }
   MPB_D static void fold(Acc& a, const In& x, int64_t) { a = rmul(a, cvt<Acc>(x)); }
+  MPB_D static void fold_seq(Acc& a, const In& x, int64_t i) { fold(a, x, i); }
   MPB_D static Acc merge(const Acc& l, const Acc& r) { return rmul(l, r); }
 };
 template <class V> MPB_D V lowest();
@@ -90,6 +94,7 @@ struct PArg {
   using In = TIn;
   using Acc = ArgAcc<V>;
   static constexpr bool kArg = true;
+  static constexpr bool kExt = false;
   MPB_D static Acc ident() { return Acc{IS_MAX ? lowest<V>() : highest<V>(), INT64_MAX}; }
   MPB_D static bool better(V v, int64_t i, const Acc& a) {
     return IS_MAX ? (v > a.v || (v == a.v && i < a.i)) : (v < a.v || (v == a.v && i < a.i));
@@ -97,6 +102,13 @@ struct PArg {
   MPB_D static void fold(Acc& a, const In& x, int64_t idx) {
     const V v = cvt<V>(x);
     if (better(v, idx, a)) a = Acc{v, idx};
+  }
+  // Fold for a traversal in increasing index order: an equal value can only
+  // win while nothing has been taken yet, so no index comparison is needed.
+  MPB_D static void fold_seq(Acc& a, const In& x, int64_t idx) {
+    const V v = cvt<V>(x);
+    if (IS_MAX ? (v > a.v || (v == a.v && a.i == INT64_MAX)) : (v < a.v || (v == a.v && a.i == INT64_MAX)))
+      a = Acc{v, idx};
   }
   MPB_D static Acc merge(const Acc& l, const Acc& r) { return better(r.v, r.i, l) ? r : l; }
   // NaN-ignoring extreme of two values (fmax/fmin return the non-NaN one).
@@ -116,6 +128,27 @@ struct PArg {
   MPB_D static bool improves(V m, const Acc& a, int64_t first) {
     return IS_MAX ? (m > a.v || (m == a.v && first < a.i)) : (m < a.v || (m == a.v && first < a.i));
   }
+};
+
+// max / min values alone (no index): the CPU loop keeps the first element
+// and replaces it only by a strictly greater (smaller) one, so its result is
+//  * NaN when the first element is NaN (write_out applies that rule),
+//  * otherwise the extremum of the non-NaN elements, which fmax/fmin give in
+//    any order, except for the sign of a zero result: equal values never
+//    replace the accumulator, so a zero extremum carries the sign of the first
+//    zero in index order. Kernels settle that case by a rescan
+//    (ext_zero_fix_*), which runs only for outputs whose extremum is zero.
+template <class TIn, class V, bool IS_MAX>
+struct PExt {
+  using In = TIn;
+  using Acc = V;
+  static constexpr bool kArg = false;
+  static constexpr bool kExt = true;
+  MPB_D static Acc ident() { return IS_MAX ? lowest<V>() : highest<V>(); }
+  MPB_D static V pick(V a, V b) { return PArg<TIn, V, IS_MAX>::pick(a, b); }
+  MPB_D static void fold(Acc& a, const In& x, int64_t) { a = pick(a, cvt<V>(x)); }
+  MPB_D static void fold_seq(Acc& a, const In& x, int64_t i) { fold(a, x, i); }
+  MPB_D static Acc merge(const Acc& l, const Acc& r) { return pick(l, r); }
 };
 
 template <class P>
@@ -206,6 +239,14 @@ MPB_D void write_out(void* out, int64_t o, typename P::Acc acc, const RedOut& ro
     } else {
       store_dyn(out, i, ro.out_dt, acc.v);
     }
+  } else if constexpr (P::kExt) {
+    if constexpr (!std::is_same<typename P::Acc, int64_t>::value) {
+      if (ro.nan_rule && is_nan_v(cvt<typename P::Acc>(*first))) {
+        store_dyn(out, i, ro.out_dt, *first);
+        return;
+      }
+    }
+    store_dyn(out, i, ro.out_dt, acc);
   } else {
     if (ro.mode == 1)
       store_dyn(out, i, ro.out_dt, mean_div(acc, ro.count));
@@ -252,6 +293,66 @@ MPB_D void red_off(const RedDev& g, int64_t f, int64_t& off, int64_t& lidx) {
     off += c * g.rst[d];
     lidx += c * g.rw[d];
   }
+}
+
+// ------------------------------------------- zero extremum sign (PExt)
+// Smallest logical index among the zero elements of output o's segment,
+// scanned by `n` cooperating threads (thread t takes elements t, t+n, ...);
+// returns the index and whether that zero is negative.
+template <class P>
+MPB_D void first_zero_scan(const typename P::In* __restrict__ seg, const RedDev& g, int t, int n, int64_t& best,
+                           bool& neg) {
+  best = INT64_MAX;
+  neg = false;
+  for (int64_t f = t; f < g.L; f += n) {
+    int64_t off, lidx;
+    red_off(g, f, off, lidx);
+    const typename P::Acc v = cvt<typename P::Acc>(seg[off]);
+    if (v == 0 && lidx < best) {
+      best = lidx;
+      neg = signbit(v);
+    }
+  }
+}
+template <class V> MPB_D V signed_zero(bool neg) { return neg ? -V(0) : V(0); }
+
+// Warp version: all 32 lanes call it with the warp's result in lane 0.
+template <class P>
+MPB_D typename P::Acc ext_zero_fix_warp(typename P::Acc acc, const typename P::In* __restrict__ seg,
+                                        const RedDev& g, int lane) {
+  if constexpr (P::kExt && !std::is_same<typename P::Acc, int64_t>::value) {
+    acc = __shfl_sync(0xffffffffu, acc, 0);
+    if (acc == 0) {
+      int64_t best;
+      bool neg;
+      first_zero_scan<P>(seg, g, lane, 32, best, neg);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const int64_t ob = shfl_dn(best, o);
+        const bool on = __shfl_down_sync(0xffffffffu, (int)neg, o) != 0;
+        if (ob < best) {
+          best = ob;
+          neg = on;
+        }
+      }
+      acc = signed_zero<typename P::Acc>(neg);
+    }
+  }
+  return acc;
+}
+// Single-thread version.
+template <class P>
+MPB_D typename P::Acc ext_zero_fix_thread(typename P::Acc acc, const typename P::In* __restrict__ seg,
+                                          const RedDev& g) {
+  if constexpr (P::kExt && !std::is_same<typename P::Acc, int64_t>::value) {
+    if (acc == 0) {
+      int64_t best;
+      bool neg;
+      first_zero_scan<P>(seg, g, 0, 1, best, neg);
+      acc = signed_zero<typename P::Acc>(neg);
+    }
+  }
+  return acc;
 }
 
 // ------------------------------------------------- ROW: warp per output
@@ -346,6 +447,7 @@ __global__ void __launch_bounds__(kRedThreads) k_red_row_warp(const typename P::
         fold_segment_scalar<P>(acc, a + base + so, g.Li, sl, rwi, 0, g.Li, 32, lane);
     }
     acc = warp_reduce<P>(acc);
+    acc = ext_zero_fix_warp<P>(acc, a + base, g, lane);
     if (lane == 0) write_out<P>(out, o, acc, ro, a + base);
   }
 }
@@ -385,6 +487,7 @@ __global__ void __launch_bounds__(kRedThreads) k_red_row_block(const typename P:
       }
     }
     acc = block_reduce<P>(acc);
+    if (!partial && threadIdx.x < 32) acc = ext_zero_fix_warp<P>(acc, a + base, g, threadIdx.x);
     if (threadIdx.x == 0) {
       if (partial)
         scratch[o * S + sx] = acc;
@@ -410,17 +513,19 @@ __global__ void __launch_bounds__(kRedThreads) k_red_col(const typename P::In* _
     const int64_t base = kept_off(g, o);
     typename P::Acc acc = P::ident();
     if (g.R == 1) {
+      // one reduced dim walked in increasing index order
       const int64_t st = g.rst[0], w = g.rw[0];
-      constexpr int UNR = 8;
+      constexpr int UNR = 16;
       int64_t f = f0;
-      for (; f + UNR <= f1; f += UNR) {
+      const typename P::In* ap = a + base + f0 * st;
+      for (; f + UNR <= f1; f += UNR, ap += UNR * st) {
         typename P::In v[UNR];
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) v[u] = a[base + (f + u) * st];
+        for (int u = 0; u < UNR; ++u) v[u] = ap[u * st];
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) P::fold(acc, v[u], (f + u) * w);
+        for (int u = 0; u < UNR; ++u) P::fold_seq(acc, v[u], (f + u) * w);
       }
-      for (; f < f1; ++f) P::fold(acc, a[base + f * st], f * w);
+      for (; f < f1; ++f, ap += st) P::fold_seq(acc, *ap, f * w);
     } else {
       int64_t c[kMaxCollapsed];
       int64_t rem = f0, off = 0, lidx = 0;
@@ -446,7 +551,7 @@ __global__ void __launch_bounds__(kRedThreads) k_red_col(const typename P::In* _
     if (partial)
       scratch[(int64_t)sx * g.M + o] = acc;
     else
-      write_out<P>(out, o, acc, ro, a + base);
+      write_out<P>(out, o, ext_zero_fix_thread<P>(acc, a + base, g), ro, a + base);
   }
 }
 
@@ -465,7 +570,9 @@ __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::I
       typename P::Acc acc = P::ident();
       for (int j = lane; j < S; j += 32) acc = P::merge(acc, part[o * S + j]);
       acc = warp_reduce<P>(acc);
-      if (lane == 0) write_out<P>(out, o, acc, ro, a + kept_off(g, o));
+      const int64_t base = kept_off(g, o);
+      acc = ext_zero_fix_warp<P>(acc, a + base, g, lane);
+      if (lane == 0) write_out<P>(out, o, acc, ro, a + base);
     }
   } else {
     const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -473,7 +580,8 @@ __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::I
     for (int64_t o = gt; o < g.M; o += gs) {
       typename P::Acc acc = part[o];
       for (int j = 1; j < S; ++j) acc = P::merge(acc, part[(int64_t)j * g.M + o]);
-      write_out<P>(out, o, acc, ro, a + kept_off(g, o));
+      const int64_t base = kept_off(g, o);
+      write_out<P>(out, o, ext_zero_fix_thread<P>(acc, a + base, g), ro, a + base);
     }
   }
 }
@@ -494,6 +602,7 @@ __global__ void __launch_bounds__(kRedThreads) k_red_gen(const typename P::In* _
       P::fold(acc, a[base + off], lidx);
     }
     acc = warp_reduce<P>(acc);
+    acc = ext_zero_fix_warp<P>(acc, a + base, g, lane);
     if (lane == 0) write_out<P>(out, o, acc, ro, a + base);
   }
 }
@@ -581,6 +690,7 @@ int launch_policy(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s)
 int run_sum(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s);
 int run_prod(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s);
 int run_arg(const RedReq& r, const RedPlan& pl, RedOut ro, bool is_max, cudaStream_t s);
+int run_ext(const RedReq& r, const RedPlan& pl, RedOut ro, bool is_max, cudaStream_t s);
 
 }  // namespace red
 }  // namespace mpb

@@ -26,7 +26,7 @@ import torch
 from . import dtypes as _dt
 from . import errors
 from ._lib import LIB, OPS, RED_OPS, check, i64arr
-from .array import Array, contiguous_strides, empty, parse_device
+from .array import Array, contiguous_strides, empty, parse_device, reshape
 
 _ARITH_OK = {_dt.F32, _dt.F64, _dt.C64, _dt.C128, _dt.F16, _dt.BF16}
 _UNARY_OK = {_dt.F32, _dt.F64, _dt.F16, _dt.BF16}
@@ -362,6 +362,18 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
     axes = _resolve_axes(axis, a.ndim)
     if len(axes) > 1 and out is not None:
         raise errors.ShapeError("reduction with multiple axes does not support out= yet")
+    if (kernel in ("max", "min") and axis is not None and len(axes) > 1
+            and a.dtype.code in (_dt.F16, _dt.BF16, _dt.F32, _dt.F64)):
+        # reduce_multi (reduction.rs:118-223) reduces one axis at a time, in
+        # ascending order. For float max/min that order is visible: a NaN at
+        # the start of an inner run, or the sign of a zero extremum, decides
+        # the outcome per pass, so the passes are kept.
+        cur = a
+        for ax in sorted(axes):
+            cur = _reduce(kernel, cur, ax, True, None)
+        if keepdims:
+            return cur
+        return reshape(cur, tuple(s for i, s in enumerate(a.shape) if i not in axes))
     red = axes if axes else list(range(a.ndim))
     is_arg = kernel in ("argmax", "argmin")
     cd = _compute_dtype(a.dtype, kernel)

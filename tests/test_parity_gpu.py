@@ -327,6 +327,41 @@ def test_reduce_nan_ties_signed_zero(ms, oracle):
             assert_bits_equal(getattr(ms, op)(dev(ms, m), axis=axis).numpy(), oracle.reduce(op, m, axis), f"{op} {axis}")
 
 
+@pytest.mark.parametrize("shape,axis", RED_SHAPES)
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.float16])
+def test_reduce_zero_extremum_sign(ms, oracle, shape, axis, dtype):
+    """max over non-positive data (min over non-negative data) whose zeros are
+    a random mix of +0 and -0: the result carries the sign of the first zero in
+    index order, through every kernel kind (row, block, split, column, gather)."""
+    rng = np.random.default_rng(16)
+    x = -np.abs(rng.standard_normal(shape)).astype(dtype)
+    z = rng.random(shape) < 0.02
+    x[z] = np.where(rng.random(int(z.sum())) < 0.5, -0.0, 0.0).astype(dtype)
+    for op, v in (("max", x), ("min", -x)):
+        got = getattr(ms, op)(dev(ms, v), axis=axis).numpy()
+        # the CPU path returns f32 for f16 input; the extremum is an input value
+        want = oracle.reduce(op, v, axis).astype(got.dtype)
+        assert_bits_equal(got, want, f"{op} {shape} {axis}")
+
+
+@pytest.mark.parametrize("axis", [(0, 2), (1, 2), (0, 1), (0, 1, 2)])
+def test_reduce_multi_axis_nan_runs(ms, oracle, axis):
+    """max/min over several axes reduce one axis at a time (reduction.rs:118-223):
+    a NaN at the start of an inner run hides that run from the next pass."""
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal((6, 7, 9)).astype(np.float32)
+    x[0, :, 3] = np.nan
+    x[2, 4, 0] = np.nan
+    x[:, 0, 5] = np.nan
+    x[1, 1, 1] = 50.0
+    x[0, 2, 0] = -0.0
+    for op in ("max", "min"):
+        got = getattr(ms, op)(dev(ms, x), axis=axis).numpy()
+        assert_bits_equal(got, oracle.reduce(op, x, axis), f"{op} {axis}")
+        got = getattr(ms, op)(dev(ms, x), axis=axis, keepdims=True).numpy()
+        assert_bits_equal(got, oracle.reduce(op, x, axis, keepdims=True), f"{op} {axis} keepdims")
+
+
 @pytest.mark.parametrize("dtype", [np.int64, np.int32, np.int8, np.uint8, np.bool_])
 def test_reduce_int_exact(ms, oracle, dtype):
     rng = np.random.default_rng(16)
@@ -406,3 +441,32 @@ def test_empty_and_scalar(ms, oracle):
     s = dev(ms, np.array(3.0, np.float32))
     assert ms.add(s, s).item() == 6.0
     assert ms.cumsum(e).shape == (0,)
+
+
+@pytest.mark.parametrize("op", ["sin", "cos", "exp", "log"])
+def test_transcendental_special_values_f32(ms, oracle, op):
+    """Edges of the float sin/cos/exp/log evaluation: signed zeros, inf, NaN,
+    subnormals, arguments past the 2^20 reduction limit, exp's overflow and
+    underflow thresholds, log near 1."""
+    v = [0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 1e-38, 3.4e38, -3.4e38, 1048575.9, 1048576.0,
+         -1048577.0, 1e7, 12345678.0, 88.72, 88.73, 89.0, -87.3, -103.97, -103.98, -104.0, -150.0,
+         1.0, 1.0000001, 0.99999994, 2.0, 0.5, np.pi / 2, np.pi, 3 * np.pi / 2, 1e-20, 710.0]
+    x = np.array(v, np.float32)
+    x = np.concatenate([x, np.random.default_rng(30).standard_normal(4096).astype(np.float32) * 1e5])
+    got = getattr(ms, op)(dev(ms, x)).numpy()
+    want = oracle.unary(op, x)
+    assert_ulp(got, want, 2, op + " specials")
+    zero = want == 0
+    assert np.array_equal(np.signbit(got[zero]), np.signbit(want[zero])), op + ": signed zero"
+    # the same inputs through the two-element (packed) path: contiguous, even length
+    x2 = np.ascontiguousarray(np.repeat(x, 2))
+    got2 = getattr(ms, op)(dev(ms, x2)).numpy()
+    assert_bits_equal(got2[0::2], got, op + " paired vs single")
+
+
+def test_f16_pow_special_values(ms, oracle):
+    v = np.array([0.0, -0.0, 1.0, -1.0, 2.0, -2.0, 0.5, 65504.0, 6e-8, np.inf, -np.inf, np.nan, 3.0, -3.0],
+                 np.float16)
+    a, b = np.meshgrid(v, v)
+    got = ms.pow(dev(ms, a), dev(ms, b)).numpy()
+    assert_ulp(got, oracle.binary("pow", a, b), 2, "f16 pow specials")
