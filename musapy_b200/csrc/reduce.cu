@@ -180,17 +180,34 @@ int red_plan(const RedReq& r, RedPlan& pl) {
     }
   } else if (col || (row && pl.Li < 32)) {
     pl.kind = RK_COL;
-    const int64_t want = (int64_t)sms * 1024;
-    if (pl.M < want && pl.L >= 256) {
-      int64_t S = cdiv(want, pl.M);
-      if (S > pl.L / 64) S = pl.L / 64;
-      if (S > 65535) S = 65535;
-      if (S > 1) {
-        pl.kind = RK_COL_SPLIT;
-        pl.splits = S;
-        pl.chunk = cdiv(pl.L, S);
-        pl.splits = cdiv(pl.L, pl.chunk);
+    // Thread per output: a block of 256 outputs walks its whole chunk of the
+    // reduced dim, so a block's time is proportional to the chunk length and
+    // the pass takes ceil(w) "waves" of w = blocks * S / capacity. Splitting
+    // the reduced dim into S chunks trades that wave quantisation (a grid of
+    // 1.15 waves runs at 58%) against the combine pass, which moves 32 bytes
+    // per (output, split). S minimises
+    //   data_bytes * ceil(w) / w + 32 * M * S
+    // with capacity = 6 blocks per SM (the column kernels use <= 40 registers)
+    // and chunks of at least 64 elements.
+    const int64_t blocks = cdiv(pl.M, 256);
+    const double cap = 6.0 * sms;
+    const double data = (double)pl.M * (double)pl.L * (double)esz;
+    int64_t s_max = pl.L / 64;
+    if (s_max > 4096) s_max = 4096;
+    int64_t best_s = 1;
+    double best_cost = 0.0;
+    for (int64_t S = 1; S <= (s_max > 1 ? s_max : 1); ++S) {
+      const double w = (double)(blocks * S) / cap;
+      const double cost = data * ceil(w) / w + (S > 1 ? 32.0 * (double)pl.M * (double)S : 0.0);
+      if (S == 1 || cost < best_cost) {
+        best_cost = cost;
+        best_s = S;
       }
+    }
+    if (best_s > 1) {
+      pl.kind = RK_COL_SPLIT;
+      pl.chunk = cdiv(pl.L, best_s);
+      pl.splits = cdiv(pl.L, pl.chunk);
     }
   } else {
     pl.kind = RK_GEN;
