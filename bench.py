@@ -416,6 +416,8 @@ def config_inputs(name: str):
 def run_suite(args) -> None:
     import gc
 
+    import numpy as np
+
     import torch
 
     import musapy_b200 as ms
@@ -536,6 +538,43 @@ def run_suite(args) -> None:
         z = ms.mul(z1, z2)
         emit("C4", "mul c64 2^27", (1 << 27) * 24, lambda: ms.mul(z1, z2, out=z))
         del z1, z2, z, d
+    if "NEXT" in cfgs:
+        # the survey's "next" rows: contiguous copies of views, creation
+        # kernels, host <-> device transfers (device-side bytes = read + write)
+        q = 16384
+        x = ms.arange(q * q, dtype="f32")
+        x2 = ms.reshape(x, (q, q))
+        t = ms.contiguous(ms.transpose(x2))
+        emit("NEXT", "contiguous(transpose) f32 (16384,16384)", 2 * q * q * 4,
+             lambda: ms.contiguous(ms.transpose(x2), out=t))
+        f = ms.contiguous(ms.flip(x, 0))
+        emit("NEXT", "contiguous(flip) f32 2^28", 2 * q * q * 4, lambda: ms.contiguous(ms.flip(x, 0), out=f))
+        w = ms.reshape(x, (q // 2, 2 * q))
+        half = ms.contiguous(ms.slice(w, [[0, q // 2, 1], [0, 2 * q, 2]]))
+        emit("NEXT", "contiguous(x[:, ::2]) f32 (8192,32768)->(8192,16384)", 2 * (q * q // 2) * 4,
+             lambda: ms.contiguous(ms.slice(w, [[0, q // 2, 1], [0, 2 * q, 2]]), out=half))
+        del t, f, half, w, x2
+        n = 1 << 30
+        emit("NEXT", "arange f32 2^30", n * 4, lambda: ms.arange(0, n, 1, dtype="f32"))
+        emit("NEXT", "linspace f64 2^28", (1 << 28) * 8, lambda: ms.linspace(-1.0, 1.0, 1 << 28))
+        emit("NEXT", "eye f32 (32768,32768)", 32768 * 32768 * 4, lambda: ms.eye(32768, dtype="f32"))
+        host = np.ones(1 << 28, dtype=np.float32)
+        import time as _time
+
+        for name, fn in (("from_numpy 1 GiB f32 (pageable host)", lambda: ms.from_numpy(host)),
+                         ("Array.numpy() 1 GiB f32", lambda: x.numpy())):
+            fn()
+            torch.cuda.synchronize()
+            t0 = _time.perf_counter()
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            dt_ms = (_time.perf_counter() - t0) / 3 * 1e3
+            nb = (1 << 28) * 4
+            print(json.dumps({"config": "NEXT", "op": name, "ms": round(dt_ms, 3),
+                              "gbs": round(nb / (dt_ms * 1e-3) / 1e9, 2), "bytes": nb,
+                              "note": "wall clock, PCIe-bound"}), flush=True)
+        del x, host
     gc.collect()
     torch.cuda.empty_cache()
 
@@ -550,7 +589,7 @@ def main() -> None:
     ap.add_argument("--sample-rows", type=int, default=2048, help="rows of the CPU sample")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--suite", default="", help="comma list of C1..C4: time every op of those configs")
+    ap.add_argument("--suite", default="", help="comma list of C1..C4, NEXT: time every op of those configs")
     args = ap.parse_args()
     if args.suite:
         run_suite(args)

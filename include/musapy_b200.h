@@ -161,6 +161,28 @@ int mpb_cumsum(int ndim, const int64_t* shape, const int64_t* strides, const voi
  * its scratch: MPB_OK, or MPB_ERR_TIMEOUT when a bounded wait gave up. */
 int mpb_cumsum_status(const void* scratch, mpb_stream_t stream);
 
+/* ---------------------------------------------------------------- creation */
+
+/* Fills `out` (n contiguous elements of `dtype`) with start + i*step, each
+ * value evaluated in f64 (multiply, then add, each rounded) and converted once
+ * with Rust `as` semantics, as the CPU path of ms.arange does
+ * (creation.rs:469-501 and :324-348). Replaces musapy_arange_{f32,f64,i64,i32}
+ * (kernels.rs, init.mu:86-97), which compute in the element type; every dtype
+ * is accepted. The caller derives n from start/stop/step (arange_len,
+ * creation.rs:624-633). */
+int mpb_arange(void* out, int dtype, int64_t n, double start, double step, mpb_stream_t stream);
+
+/* n evenly spaced values from start to stop inclusive: step = (stop - start) /
+ * (n - 1) in f64, element i = start + i*step as in mpb_arange; n == 1 gives
+ * start (creation.rs:508-521 and :350-377). Replaces musapy_linspace_{f32,f64}
+ * (init.mu:102-115). */
+int mpb_linspace(void* out, int dtype, int64_t n, double start, double stop, mpb_stream_t stream);
+
+/* rows x cols matrix (C-contiguous) of zeros with ones where col - row == k
+ * (creation.rs:457-461, init.mu:47-56). Replaces musapy_eye_{f32,f64,i64,i32}
+ * (init.mu:121-134); every dtype is accepted. */
+int mpb_eye(void* out, int dtype, int64_t rows, int64_t cols, int64_t k, mpb_stream_t stream);
+
 /* ---------------------------------------------------- axis-0 sharding (new) */
 
 /* Device combine of per-rank argmax/argmin records (MPB_R_ARG*_REC output,

@@ -49,6 +49,7 @@ from .dtypes import (
     uint32,
     uint64,
 )
+from .streams import Stream, device, dtype, stream
 from .errors import (
     DeviceError,
     DeviceNotConfiguredError,
@@ -64,6 +65,7 @@ from .errors import (
 from .ops import (
     abs,
     add,
+    arange,
     argmax,
     argmin,
     astype,
@@ -74,10 +76,12 @@ from .ops import (
     div,
     eq,
     exp,
+    eye,
     full,
     ge,
     gt,
     le,
+    linspace,
     log,
     lt,
     max,
@@ -100,10 +104,6 @@ from .ops import (
 
 __version__ = "0.1.0"
 bool = bool_  # noqa: A001 - musapy exports its bool dtype under this name
-
-
-def dtype(spec) -> Dtype:
-    return _dtype_mod.parse(spec)
 
 
 def library_path() -> str:

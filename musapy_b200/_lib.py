@@ -48,7 +48,7 @@ RED_KINDS = {0: "empty", 1: "row_warp", 2: "row_block", 3: "row_split", 4: "col"
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m musapy_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python musapy_b200/build.py` "
             "(musapy_b200 has no CPU fallback)"
         )
     L = ctypes.CDLL(LIB_PATH)
@@ -100,6 +100,12 @@ def _load() -> ctypes.CDLL:
     L.mpb_shard_arg_combine.argtypes = [c_vp, ctypes.c_int, c_i64p, ctypes.c_int, ctypes.c_int, c_vp, c_vp, c_vp]
     L.mpb_shard_sum_finalize.restype = ctypes.c_int
     L.mpb_shard_sum_finalize.argtypes = [c_vp, ctypes.c_double, ctypes.c_int, c_vp, c_vp, c_vp]
+    L.mpb_arange.restype = ctypes.c_int
+    L.mpb_arange.argtypes = [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_double, c_vp]
+    L.mpb_linspace.restype = ctypes.c_int
+    L.mpb_linspace.argtypes = [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_double, c_vp]
+    L.mpb_eye.restype = ctypes.c_int
+    L.mpb_eye.argtypes = [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, c_vp]
     return L
 
 

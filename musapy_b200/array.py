@@ -14,6 +14,7 @@ import torch
 
 from . import dtypes as _dt
 from . import errors
+from . import streams as _streams
 
 _DEFAULT_DEVICE = [0]
 _DEFAULT_DTYPE = [_dt.float32]
@@ -63,7 +64,7 @@ class Device:
 
 def parse_device(spec) -> int:
     if spec is None:
-        return _DEFAULT_DEVICE[0]
+        return _streams.default_device()
     if isinstance(spec, Device):
         return spec.index
     if isinstance(spec, torch.device):
@@ -97,7 +98,8 @@ def set_default_dtype(spec) -> None:
 
 
 def default_dtype() -> _dt.Dtype:
-    return _DEFAULT_DTYPE[0]
+    """The innermost ``ms.dtype`` context's dtype, else the global default."""
+    return _streams.default_dtype()
 
 
 def contiguous_strides(shape: Sequence[int]) -> tuple:
@@ -197,7 +199,15 @@ class Array:
         return self._buf.data_ptr() + self._offset * self._dtype.itemsize
 
     def _stream(self) -> int:
-        return torch.cuda.current_stream(self._dev).cuda_stream
+        return _streams.current_stream(self._dev).cuda_stream
+
+    @property
+    def stream(self):
+        """The stream the array was created on (array.rs:73); for arrays that
+        wrap foreign memory, the stream that last used it, else the current
+        stream of its device."""
+        ts = getattr(self._buf, "_mpb_owner", None) or getattr(self._buf, "_mpb_stream", None)
+        return _streams._wrap(self._dev, ts) if ts is not None else _streams.current_stream(self._dev)
 
     def __len__(self) -> int:
         if not self._shape:
@@ -212,6 +222,7 @@ class Array:
         if n == 0:
             return np.zeros(a._shape, dtype=_dt.to_numpy(a._dtype))
         start = a._offset * a._dtype.itemsize
+        _streams.launch("numpy", a._dev, a)
         host = a._buf.narrow(0, start, n).cpu().numpy()
         return host.view(_dt.to_numpy(a._dtype)).reshape(a._shape)
 
@@ -362,6 +373,7 @@ def empty(shape, dtype=None, device=None) -> Array:
     n = _prod(shape) * d.itemsize
     # Round allocations up to 16 bytes so every buffer start is vector aligned.
     buf = torch.empty(max(16, (n + 15) // 16 * 16), dtype=torch.uint8, device=f"cuda:{dev}")
+    buf._mpb_owner = _streams.current_stream(dev).torch_stream  # the stream the array belongs to
     return Array(buf, shape, contiguous_strides(shape), 0, d, dev)
 
 
@@ -379,11 +391,13 @@ def from_numpy(arr: np.ndarray, device=None, dtype=None) -> Array:
     d = _dt.from_numpy(arr.dtype) if dtype is None else _dt.parse(dtype)
     if _dt.to_numpy(d) != arr.dtype:
         arr = _np_cast(arr, d)
-    arr = np.ascontiguousarray(arr)
+    if not arr.flags.c_contiguous:  # (np.ascontiguousarray would turn 0-d into 1-d)
+        arr = arr.copy(order="C")
     out = empty(arr.shape, d, device)
     n = arr.nbytes
     if n:
         src = torch.from_numpy(arr.reshape(-1).view(np.uint8))
+        _streams.launch("from_numpy", out._dev, out)
         out._buf[:n].copy_(src)
     return out
 

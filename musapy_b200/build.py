@@ -6,7 +6,10 @@ rebuilt only when a source or header is newer than the object, so repeated
 calls are cheap. The CUDA runtime is linked dynamically, so the library
 shares one runtime (and one error state) with the host process.
 
-Usage:  python -m musapy_b200.build [--force] [--jobs N]
+Usage:  python musapy_b200/build.py [--force] [--jobs N]
+
+Run it as a script (it needs only the standard library): importing the
+package loads the library, which may be missing or stale before a build.
 """
 from __future__ import annotations
 

@@ -18,6 +18,7 @@ wraps the output. Differences from the reference, all deliberate:
 from __future__ import annotations
 
 import builtins
+import math
 import numbers
 
 import numpy as np
@@ -25,6 +26,7 @@ import torch
 
 from . import dtypes as _dt
 from . import errors
+from . import streams as _streams
 from ._lib import LIB, OPS, RED_OPS, check, i64arr
 from .array import Array, contiguous_strides, empty, parse_device, reshape
 
@@ -33,7 +35,14 @@ _UNARY_OK = {_dt.F32, _dt.F64, _dt.F16, _dt.BF16}
 
 
 def _stream(dev: int) -> int:
-    return torch.cuda.current_stream(dev).cuda_stream
+    return _streams.current_stream(dev).cuda_stream
+
+
+def _launch(op: str, dev: int, *arrays) -> int:
+    """CUDA stream for a launch of `op` touching `arrays` on `dev`: waits for
+    other streams' pending work on those buffers, checks the stream is not
+    poisoned and records the op context (streams.launch)."""
+    return _streams.launch(op, dev, *arrays)
 
 
 def _scalar_like(x, other: Array) -> Array:
@@ -94,14 +103,6 @@ def _alias(out: Array, *ins: Array) -> bool:
     return any(out._buf.untyped_storage().data_ptr() == x._buf.untyped_storage().data_ptr() for x in ins)
 
 
-def _record(dev: int, *arrs: Array) -> None:
-    """Keep buffers alive for the stream that uses them when it is not the
-    one they were allocated on (musapy's read/write events, buffer.rs:225-326)."""
-    s = torch.cuda.current_stream(dev)
-    for x in arrs:
-        x._buf.record_stream(s)
-
-
 def _same_device(name: str, *arrs: Array) -> int:
     dev = arrs[0]._dev
     for x in arrs[1:]:
@@ -134,7 +135,7 @@ def _binary(name: str, a, b, out):
         OPS[name], n, i64arr(shape),
         a.data_ptr, a.dtype.code, i64arr(_bstrides(a, shape)),
         b.data_ptr, b.dtype.code, i64arr(_bstrides(b, shape)),
-        res.data_ptr, d.code, d.code, 0.0, 0.0, _stream(dev),
+        res.data_ptr, d.code, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
     )
     check(rc, name)
     return res
@@ -180,7 +181,7 @@ def _compare(name: str, a, b, out):
         OPS[name], len(shape), i64arr(shape),
         a.data_ptr, a.dtype.code, i64arr(_bstrides(a, shape)),
         b.data_ptr, b.dtype.code, i64arr(_bstrides(b, shape)),
-        res.data_ptr, _dt.BOOL, d.code, 0.0, 0.0, _stream(dev),
+        res.data_ptr, _dt.BOOL, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
     )
     check(rc, name)
     return res
@@ -232,7 +233,7 @@ def _unary(name: str, a: Array, out, p0: float = 0.0, p1: float = 0.0):
         res = empty(a.shape, out_d, dev)
     rc = LIB.mpb_elementwise(
         OPS[name], a.ndim, i64arr(a.shape), a.data_ptr, d.code, i64arr(a.strides),
-        None, 0, None, res.data_ptr, out_d.code, d.code, float(p0), float(p1), _stream(dev),
+        None, 0, None, res.data_ptr, out_d.code, d.code, float(p0), float(p1), _launch(name, dev, a, res),
     )
     check(rc, name)
     return res
@@ -289,7 +290,7 @@ def _cast_into(a: Array, d: _dt.Dtype, out: Array | None = None) -> Array:
     res = out if out is not None else empty(a.shape, d, dev)
     rc = LIB.mpb_elementwise(
         OPS["cast"], a.ndim, i64arr(a.shape), a.data_ptr, a.dtype.code, i64arr(a.strides),
-        None, 0, None, res.data_ptr, d.code, d.code, 0.0, 0.0, _stream(dev),
+        None, 0, None, res.data_ptr, d.code, d.code, 0.0, 0.0, _launch("cast", dev, a, res),
     )
     check(rc, "cast")
     return res
@@ -307,8 +308,17 @@ def astype(a: Array, dtype, out=None) -> Array:
     return _cast_into(a, d, out)
 
 
-def contiguous(a: Array) -> Array:
-    return _cast_into(a, a.dtype)
+def contiguous(a: Array, out=None) -> Array:
+    """``ms.contiguous`` (indexing.rs:181): a C-contiguous copy of a view
+    (tiled transpose through shared memory when the view's unit stride is on
+    an outer dim). ``out=`` receives the copy instead of a new array."""
+    if not isinstance(a, Array):
+        raise TypeError("contiguous: expected a musapy Array")
+    if out is not None:
+        _check_out(out, a.shape, a.dtype, a._dev, "contiguous")
+        if _alias(out, a):
+            raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
+    return _cast_into(a, a.dtype, out)
 
 
 # -------------------------------------------------------------- reductions
@@ -408,7 +418,8 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
             raise errors.ShapeError(f"{kernel}: zero-size reduction has no identity")
         fillv = {"sum": 0.0, "prod": 1.0, "mean": float("nan")}[kernel]
         check(LIB.mpb_elementwise(OPS["fill"], len(out_shape), i64arr(out_shape), None, 0, None, None, 0, None,
-                                  res.data_ptr, out_d.code, out_d.code, fillv, 0.0, _stream(dev)), "fill")
+                                  res.data_ptr, out_d.code, out_d.code, fillv, 0.0, _launch("fill", dev, res)),
+              "fill")
         return res
     src = _widen_int(a)
     in_code = src.dtype.code
@@ -424,7 +435,7 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
     rc = LIB.mpb_reduce(
         op, src.ndim, shape_c, strides_c, src.data_ptr, in_code, mask,
         res.data_ptr, out_d.code, cd.code, 1,
-        scratch.data_ptr() if scratch is not None else None, nbytes, _stream(dev),
+        scratch.data_ptr() if scratch is not None else None, nbytes, _launch(kernel, dev, src, res),
     )
     check(rc, kernel)
     return res
@@ -500,7 +511,7 @@ def cumsum(a, axis=None, out=None):
     nbytes = LIB.mpb_cumsum_scratch_bytes(src.ndim, shape_c, strides_c, src.data_ptr, d.code, ax, res.data_ptr, cd.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
     rc = LIB.mpb_cumsum(src.ndim, shape_c, strides_c, src.data_ptr, d.code, ax, res.data_ptr, cd.code,
-                        scratch.data_ptr() if scratch is not None else None, nbytes, _stream(dev))
+                        scratch.data_ptr() if scratch is not None else None, nbytes, _launch("cumsum", dev, src, res))
     check(rc, "cumsum")
     if scratch is not None and _CHECK_SCAN_STATUS[0]:
         check(LIB.mpb_cumsum_status(scratch.data_ptr(), _stream(dev)), "cumsum")
@@ -521,7 +532,7 @@ def full(shape, fill_value, dtype=None, device=None) -> Array:
     v = complex(fill_value)
     check(LIB.mpb_elementwise(OPS["fill"], res.ndim, i64arr(res.shape), None, 0, None, None, 0, None,
                               res.data_ptr, res.dtype.code, res.dtype.code, v.real, v.imag,
-                              _stream(res._dev)), "fill")
+                              _launch("fill", res._dev, res)), "fill")
     return res
 
 
@@ -539,3 +550,58 @@ def zeros_like(a: Array) -> Array:
 
 def ones_like(a: Array) -> Array:
     return full(a.shape, 1.0, a.dtype, a._dev)
+
+
+def _arange_len(start: float, stop: float, step: float) -> int:
+    """arange_len (creation.rs:624-633)."""
+    if step > 0.0 and start >= stop:
+        return 0
+    if step < 0.0 and start <= stop:
+        return 0
+    n = math.ceil((stop - start) / step)
+    return int(n) if n > 0 else 0
+
+
+def arange(start, stop=None, step=1, dtype=None, device=None) -> Array:
+    """``ms.arange`` (creation.rs:469-501): ``arange(stop)`` or
+    ``arange(start, stop, step)``; float64 when any argument is a Python
+    float, int64 otherwise (rust/musapy-python/src/ops.rs:752-786), unless
+    ``dtype`` is given. Element i is start + i*step evaluated in f64 and
+    converted once, as the CPU path does."""
+    any_float = any(isinstance(v, float) for v in (start, stop, step))
+    start, step = float(start), float(step)
+    if stop is None:
+        start, stop = 0.0, start
+    stop = float(stop)
+    if step == 0.0:
+        raise errors.ShapeError("arange: step must not be zero")
+    n = _arange_len(start, stop, step)
+    if dtype is None:
+        dtype = _dt.float64 if any_float else _dt.int64
+    res = empty((n,), dtype, device)
+    check(LIB.mpb_arange(res.data_ptr, res.dtype.code, n, start, step, _launch("arange", res._dev, res)), "arange")
+    return res
+
+
+def linspace(start, stop, num=50, dtype=None, device=None) -> Array:
+    """``ms.linspace`` (creation.rs:508-521): ``num`` evenly spaced values from
+    start to stop inclusive, float64 unless ``dtype`` is given."""
+    num = int(num)
+    if num < 0:
+        raise errors.ShapeError(f"linspace: num must be non-negative, got {num}")
+    res = empty((num,), _dt.float64 if dtype is None else dtype, device)
+    check(LIB.mpb_linspace(res.data_ptr, res.dtype.code, num, float(start), float(stop), _launch("linspace", res._dev, res)),
+          "linspace")
+    return res
+
+
+def eye(n, m=None, k=0, dtype=None, device=None) -> Array:
+    """``ms.eye`` (creation.rs:457-461): an (n, m) matrix with ones on the
+    diagonal shifted by k (k > 0 above, k < 0 below); m defaults to n."""
+    n = int(n)
+    m = n if m is None else int(m)
+    if n < 0 or m < 0:
+        raise errors.ShapeError(f"eye: negative shape ({n}, {m})")
+    res = empty((n, m), dtype, device)
+    check(LIB.mpb_eye(res.data_ptr, res.dtype.code, n, m, int(k), _launch("eye", res._dev, res)), "eye")
+    return res

@@ -22,6 +22,7 @@ import torch.distributed as dist
 
 from . import dtypes as _dt
 from . import errors, ops
+from . import streams as _streams
 from ._lib import LIB, RED_OPS, check, i64arr
 from .array import Array, empty
 
@@ -94,7 +95,7 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
     cd = a.dtype
     mask = (1 << a.ndim) - 1
     shape_c, strides_c = i64arr(a.shape), i64arr(a.strides)
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = _streams.current_stream(dev).cuda_stream
     nbytes = LIB.mpb_reduce_scratch_bytes(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code,
                                           mask, cd.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
@@ -128,7 +129,7 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
     src = a if a.dtype.code in (_dt.F32, _dt.F64, _dt.F16, _dt.BF16, _dt.I64, _dt.U64) else ops.astype(a, _dt.int64)
     mask = (1 << src.ndim) - 1
     shape_c, strides_c = i64arr(src.shape), i64arr(src.strides)
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = _streams.current_stream(dev).cuda_stream
     op = RED_OPS["argmax_rec" if is_max else "argmin_rec"]
     nbytes = LIB.mpb_reduce_scratch_bytes(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
                                           src.dtype.code)

@@ -1,0 +1,299 @@
+"""Streams: ``ms.Stream``, the ``ms.stream`` / ``ms.device`` / ``ms.dtype``
+context managers, cross-stream ordering and stream poisoning.
+
+musapy keeps per-buffer read/write events so that an op on one stream waits
+for the work other streams still have on its inputs and outputs
+(rust/musapy-core/src/buffer.rs:225-326, ADR L1-8), and marks a stream
+poisoned when an asynchronous fault surfaces at synchronize, reporting the
+op that was running (stream.rs:311-414). Here a stream is a CUDA stream (a
+torch.cuda.Stream, so torch's caching allocator orders frees on it) and the
+bookkeeping is per buffer: every buffer remembers the last stream that used
+it; an op on stream S touching a buffer last used on P != S makes S wait for
+P's work so far (an event recorded on P, waited on S: no host sync) and tells
+the allocator the buffer is in use on S. That orders read-after-write,
+write-after-read and write-after-write across streams.
+
+Poisoning: ``Stream.synchronize`` turns an asynchronous CUDA error into
+``StreamError`` naming the ops launched on the stream since its last
+successful synchronize (the op context), and every later op on that stream
+raises ``StreamError`` before launching anything.
+"""
+from __future__ import annotations
+
+import collections
+import itertools
+import threading
+
+import torch
+
+from . import dtypes as _dt
+from . import errors
+
+_ids = itertools.count(1)
+_tls = threading.local()
+# one Stream object per CUDA stream handle, so that ids and poison persist
+_wrappers: dict = {}
+_wrappers_lock = threading.Lock()
+
+OP_CONTEXT_DEPTH = 32
+
+
+def _stack(name: str) -> list:
+    st = getattr(_tls, name, None)
+    if st is None:
+        st = []
+        setattr(_tls, name, st)
+    return st
+
+
+class Stream:
+    """``ms.Stream(device=None, priority=0)`` (rust/musapy-python/src/stream.rs:14-90).
+
+    ``device`` defaults to the current default device ("cpu" in musapy; this
+    engine has CUDA devices only). ``priority`` is the CUDA stream priority
+    (lower is higher priority, as in CUDA)."""
+
+    def __init__(self, device=None, priority: int = 0, _torch_stream=None) -> None:
+        from .array import parse_device
+
+        self._dev = parse_device(device if device is not None else default_device())
+        self._priority = int(priority)
+        self._torch = _torch_stream if _torch_stream is not None else torch.cuda.Stream(
+            device=f"cuda:{self._dev}", priority=self._priority)
+        self._id = next(_ids)
+        self._poison = None
+        self._ops = collections.deque(maxlen=OP_CONTEXT_DEPTH)
+        with _wrappers_lock:
+            _wrappers[(self._dev, self._torch.cuda_stream)] = self
+
+    # ------------------------------------------------------------ properties
+    @property
+    def priority(self) -> int:
+        return self._priority
+
+    @property
+    def device(self):
+        from .array import Device
+
+        return Device(self._dev)
+
+    @property
+    def id(self) -> int:
+        return self._id
+
+    @property
+    def is_poisoned(self) -> bool:
+        return self._poison is not None
+
+    @property
+    def pending_count(self) -> int:
+        """Ops launched since the last synchronize that may still be running."""
+        if not self._ops:
+            return 0
+        try:
+            done = self._torch.query()
+        except RuntimeError:
+            done = False
+        return 0 if done else len(self._ops)
+
+    @property
+    def cuda_stream(self) -> int:
+        return self._torch.cuda_stream
+
+    @property
+    def torch_stream(self):
+        return self._torch
+
+    # --------------------------------------------------------------- control
+    def synchronize(self) -> None:
+        """Wait for every op on the stream; an asynchronous fault becomes
+        StreamError with the op context and poisons the stream."""
+        self.check()
+        try:
+            self._torch.synchronize()
+        except RuntimeError as e:
+            self._poison = (f"stream {self._id} on cuda:{self._dev} poisoned: {e}; ops since the last "
+                            f"synchronize: {self.op_context() or 'none recorded'}")
+            raise errors.StreamError(self._poison) from e
+        self._ops.clear()
+
+    def check(self) -> None:
+        if self._poison is not None:
+            raise errors.StreamError(self._poison)
+
+    def op_context(self) -> str:
+        return "; ".join(self._ops)
+
+    def _note(self, op: str) -> None:
+        self._ops.append(op)
+
+    def __eq__(self, other) -> bool:
+        return isinstance(other, Stream) and other._dev == self._dev and other.cuda_stream == self.cuda_stream
+
+    def __hash__(self) -> int:
+        return hash((self._dev, self.cuda_stream))
+
+    def __repr__(self) -> str:
+        return f"Stream(device=cuda:{self._dev}, priority={self._priority}, id={self._id})"
+
+
+def _wrap(dev: int, ts) -> Stream:
+    key = (dev, ts.cuda_stream)
+    with _wrappers_lock:
+        s = _wrappers.get(key)
+    if s is None:
+        s = Stream(dev, getattr(ts, "priority", 0), _torch_stream=ts)
+    return s
+
+
+def current_stream(dev: int) -> Stream:
+    """The stream ops on `dev` run on: the innermost ``ms.stream`` context for
+    that device, else torch's current stream of the device (so torch stream
+    contexts and CUDA graph capture are honoured)."""
+    for s in reversed(_stack("streams")):
+        if s._dev == dev:
+            return s
+    return _wrap(dev, torch.cuda.current_stream(dev))
+
+
+def launch(op: str, dev: int, *arrays) -> int:
+    """Prepare a launch of `op` on the current stream of `dev` touching
+    `arrays` (inputs and outputs): poison check, cross-stream waits, allocator
+    stream bookkeeping, op context. Returns the CUDA stream handle."""
+    s = current_stream(dev)
+    if s._poison is not None:
+        raise errors.StreamError(s._poison)
+    ts = s._torch
+    capturing = None
+    for x in arrays:
+        if x is None:
+            continue
+        buf = x._buf
+        last = getattr(buf, "_mpb_stream", None)
+        if last is not None and last is not ts and last.cuda_stream != ts.cuda_stream:
+            if capturing is None:
+                capturing = _capturing(ts)
+            if capturing:
+                # inside CUDA graph capture a wait on uncaptured work is not
+                # allowed; the capturing code orders its inputs beforehand
+                continue
+            ts.wait_stream(last)
+            buf.record_stream(ts)
+        if not capturing:
+            buf._mpb_stream = ts
+    s._note(op)
+    return ts.cuda_stream
+
+
+def _capturing(ts) -> bool:
+    """Is `ts` (a torch CUDA stream) capturing a CUDA graph?"""
+    try:
+        with torch.cuda.stream(ts):
+            return torch.cuda.is_current_stream_capturing()
+    except (RuntimeError, AttributeError, TypeError):
+        return False
+
+
+def mark(dev: int, *arrays) -> None:
+    """Record that `arrays` were just written on the current stream of `dev`
+    by a torch operation (a copy), without waiting on anything."""
+    ts = current_stream(dev)._torch
+    for x in arrays:
+        x._buf._mpb_stream = ts
+
+
+# ----------------------------------------------------- context managers
+class _StreamContext:
+    """``with ms.stream(s):`` (rust/musapy-python/src/lib.rs:126-131)."""
+
+    def __init__(self, stream: Stream) -> None:
+        if not isinstance(stream, Stream):
+            raise TypeError("ms.stream() expects an ms.Stream")
+        self._s = stream
+        self._torch_ctx = None
+
+    def __enter__(self) -> Stream:
+        _stack("streams").append(self._s)
+        self._torch_ctx = torch.cuda.stream(self._s._torch)
+        self._torch_ctx.__enter__()
+        return self._s
+
+    def __exit__(self, *exc) -> bool:
+        self._torch_ctx.__exit__(*exc)
+        _stack("streams").pop()
+        return False
+
+
+def stream(s: Stream) -> _StreamContext:
+    return _StreamContext(s)
+
+
+class _DeviceContext:
+    """``with ms.device("cuda:1"):`` (lib.rs:111-116): the default device
+    inside the block."""
+
+    def __init__(self, spec) -> None:
+        from .array import parse_device
+
+        self._dev = parse_device(spec)
+
+    def __enter__(self):
+        from .array import Device
+
+        _stack("devices").append(self._dev)
+        return Device(self._dev)
+
+    def __exit__(self, *exc) -> bool:
+        _stack("devices").pop()
+        return False
+
+
+def device(spec) -> _DeviceContext:
+    return _DeviceContext(spec)
+
+
+class _DtypeContext:
+    """``with ms.dtype("f64"):`` (lib.rs:119-123): the default dtype inside
+    the block. ``ms.dtype(spec).dtype`` is the parsed Dtype."""
+
+    def __init__(self, spec) -> None:
+        self.dtype = _dt.parse(spec)
+
+    def __enter__(self) -> _dt.Dtype:
+        _stack("dtypes").append(self.dtype)
+        return self.dtype
+
+    def __exit__(self, *exc) -> bool:
+        _stack("dtypes").pop()
+        return False
+
+    def __eq__(self, other) -> bool:
+        return self.dtype == other
+
+    def __hash__(self) -> int:
+        return hash(self.dtype)
+
+    def __repr__(self) -> str:
+        return f"dtype({self.dtype.name})"
+
+
+def dtype(spec) -> _DtypeContext:
+    return _DtypeContext(spec)
+
+
+def default_device() -> int:
+    st = _stack("devices")
+    if st:
+        return st[-1]
+    from .array import _DEFAULT_DEVICE
+
+    return _DEFAULT_DEVICE[0]
+
+
+def default_dtype() -> _dt.Dtype:
+    st = _stack("dtypes")
+    if st:
+        return st[-1]
+    from .array import _DEFAULT_DTYPE
+
+    return _DEFAULT_DTYPE[0]

@@ -14,6 +14,7 @@ module; the product never does.
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 import subprocess
 
@@ -314,6 +315,60 @@ def cumsum(x: np.ndarray, axis=None) -> np.ndarray:
     if x.size:
         lib().or_cumsum(cd, _ptr(x), _ptr(out), x.ndim, _i64(x.shape), _i64(_estrides(x)), axis)
     return out
+
+
+def _fill_values(vals: np.ndarray, dst: int) -> np.ndarray:
+    """f64 values converted once with Rust `as` semantics (cpu_fill_ptr)."""
+    return np.ascontiguousarray(vals.astype(np.float64)) if dst == F64 else cast(vals.astype(np.float64), dst)
+
+
+def arange_len(start: float, stop: float, step: float) -> int:
+    """arange_len (creation.rs:624-633)."""
+    if step > 0.0 and start >= stop:
+        return 0
+    if step < 0.0 and start <= stop:
+        return 0
+    n = math.ceil((stop - start) / step)
+    return int(n) if n > 0 else 0
+
+
+def arange(start, stop=None, step=1, dtype: int | None = None) -> np.ndarray:
+    """ms.arange on the CPU device (creation.rs:469-501, cpu_fill_ptr :324-348):
+    element i = start + (i as f64) * step in f64 (no fused multiply-add), then
+    `as` the dtype; float64 when any argument is a Python float, else int64
+    (the binding's inference, rust/musapy-python/src/ops.rs:752-786)."""
+    any_float = any(isinstance(v, float) for v in (start, stop, step))
+    start, step = float(start), float(step)
+    if stop is None:
+        start, stop = 0.0, start
+    stop = float(stop)
+    if step == 0.0:
+        raise ValueError("arange: step must not be zero")
+    n = arange_len(start, stop, step)
+    if dtype is None:
+        dtype = F64 if any_float else I64
+    i = np.arange(n, dtype=np.float64)
+    return _fill_values(start + i * step, dtype)
+
+
+def linspace(start, stop, num: int = 50, dtype: int | None = None) -> np.ndarray:
+    """ms.linspace on the CPU device (creation.rs:508-521, :350-377)."""
+    start, stop = float(start), float(stop)
+    dtype = F64 if dtype is None else dtype
+    if num == 1:
+        return _fill_values(np.array([start]), dtype)
+    step = (stop - start) / float(num - 1) if num > 1 else 0.0
+    i = np.arange(num, dtype=np.float64)
+    return _fill_values(start + i * step, dtype)
+
+
+def eye(n: int, m: int | None = None, k: int = 0, dtype: int = F32) -> np.ndarray:
+    """ms.eye on the CPU device (creation.rs:457-461, :378-400): 1 where
+    col - row == k."""
+    m = n if m is None else m
+    r = np.arange(n, dtype=np.int64)[:, None]
+    c = np.arange(m, dtype=np.int64)[None, :]
+    return _fill_values((c - r == k).astype(np.float64), dtype)
 
 
 def f16_bits(x: float) -> int:

@@ -103,3 +103,25 @@ def test_broadcast_strides(case):
     out = i64arr([0] * max(1, len(target)))
     LIB.mpb_broadcast_strides(len(shape), i64arr(shape), i64arr(strides), len(target), i64arr(target), out)
     assert list(out[: len(target)]) == want, f"{K.BROADCAST_SRC}:{line}"
+
+
+def _oracle_creation(oracle, kind, args, kw):
+    kw = dict(kw)
+    if "dtype" in kw:
+        kw["dtype"] = oracle.NAMES.index(long_name(kw["dtype"]))
+    return getattr(oracle, kind)(*args, **kw)
+
+
+@pytest.mark.parametrize("case", K.CREATION, ids=lambda c: c[0])
+def test_creation(oracle, case):
+    src, kind, args, kw, exp, dt, tol = case
+    got = _oracle_creation(oracle, kind, args, kw)
+    assert oracle.NAMES[oracle.code_of(got.dtype)] == long_name(dt), src
+    check_values(got, exp, tol, src)
+
+
+@pytest.mark.parametrize("case", K.CREATION_ERRORS, ids=lambda c: c[0])
+def test_creation_errors(oracle, case):
+    src, kind, args = case
+    with pytest.raises(ValueError):
+        getattr(oracle, kind)(*args)

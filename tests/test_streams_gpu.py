@@ -1,0 +1,107 @@
+"""Streams on the GPU: the reference's multi-stream acceptance cases
+(tests/python/test_stream.py:47-230, run there on cpu and musa devices) on
+CUDA streams, plus ordering checks that would fail without the automatic
+cross-stream waits."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_two_streams_independent_arrays(ms):
+    s1, s2 = ms.Stream("cuda:0"), ms.Stream("cuda:0")
+    with ms.stream(s1):
+        a = ms.array([1.0, 2.0, 3.0], dtype="f32")
+    with ms.stream(s2):
+        b = ms.array([4.0, 5.0, 6.0], dtype="f32")
+    s1.synchronize()
+    s2.synchronize()
+    assert a.tolist() == [1.0, 2.0, 3.0] and b.tolist() == [4.0, 5.0, 6.0]
+    assert a.stream == s1 and b.stream == s2
+
+
+def test_cross_stream_add_and_out(ms):
+    s1, s2 = ms.Stream("cuda:0"), ms.Stream("cuda:0")
+    with ms.stream(s1):
+        a = ms.array([1.0, 2.0, 3.0], dtype="f32")
+    with ms.stream(s2):
+        b = ms.array([4.0, 5.0, 6.0], dtype="f32")
+        out = ms.array([0.0, 0.0, 0.0], dtype="f32")
+    with ms.stream(s2):
+        c = ms.add(a, b)
+        r = ms.add(a, b, out=out)
+    s2.synchronize()
+    assert c.tolist() == [5.0, 7.0, 9.0] and out.tolist() == [5.0, 7.0, 9.0] and r is out
+
+
+def test_reader_waits_for_writer_on_other_stream(ms):
+    """A long chain of writes on s1, then a reduction on s2 of the final
+    buffer: s2 must see every write (it waits for s1's work, no host sync)."""
+    n = 1 << 24
+    s1, s2 = ms.Stream("cuda:0"), ms.Stream("cuda:0")
+    with ms.stream(s1):
+        one = ms.ones((n,), dtype="f32")
+        x = ms.zeros((n,), dtype="f32")
+        y = ms.empty((n,), dtype="f32")
+        for _ in range(40):
+            ms.add(x, one, out=y)
+            x, y = y, x
+    with ms.stream(s2):
+        total = ms.sum(x, axis=0)
+        mx = ms.max(x)
+    s2.synchronize()
+    assert total.item() == 40.0 * n and mx.item() == 40.0
+
+
+def test_writer_waits_for_reader_on_other_stream(ms):
+    """Write-after-read: s1 reads x twenty times, then s2 overwrites x; every
+    read must see the old contents."""
+    n = 1 << 24
+    s1, s2 = ms.Stream("cuda:0"), ms.Stream("cuda:0")
+    x = ms.full((n,), 2.0, dtype="f32")
+    with ms.stream(s1):
+        sums = [ms.sum(x, axis=0) for _ in range(20)]
+    with ms.stream(s2):
+        zero = ms.zeros((n,), dtype="f32")
+        ms.mul(zero, zero, out=x)
+    s1.synchronize()
+    s2.synchronize()
+    assert all(v.item() == 2.0 * n for v in sums)
+    assert ms.max(x).item() == 0.0
+
+
+def test_interleaved_and_many_streams(ms):
+    streams = [ms.Stream("cuda:0") for _ in range(8)]
+    vals = []
+    for i, s in enumerate(streams):
+        with ms.stream(s):
+            a = ms.full((1000,), float(i), dtype="f64")
+            vals.append(ms.sum(ms.mul(a, a), axis=0))
+    for s in streams:
+        s.synchronize()
+    assert [v.item() for v in vals] == [1000.0 * i * i for i in range(8)]
+    for s in streams:
+        assert not s.is_poisoned and s.pending_count == 0
+
+
+def test_stream_reuse_after_sync_and_priority(ms):
+    hi = ms.Stream("cuda:0", priority=-1)
+    assert hi.priority == -1 and hi.device == "cuda:0"
+    with ms.stream(hi):
+        a = ms.arange(10, dtype="f32")
+    hi.synchronize()
+    with ms.stream(hi):
+        b = ms.cumsum(a)
+    hi.synchronize()
+    assert b.tolist() == np.cumsum(np.arange(10, dtype=np.float32)).tolist()
+
+
+def test_default_stream_ops_follow_torch_current_stream(ms):
+    import torch
+
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        a = ms.arange(4, dtype="f32")
+        assert ms.streams.current_stream(0).cuda_stream == side.cuda_stream
+    torch.cuda.synchronize()
+    assert a.tolist() == [0.0, 1.0, 2.0, 3.0]
