@@ -7,6 +7,9 @@
 // geometry (ew_host.cuh), for every dtype combination, and type promotion is
 // fused into the loads instead of materialising a cast temporary
 // (rust/musapy-ops/src/op_builder.rs:410-417).
+#include <map>
+#include <mutex>
+#include <utility>
 #include "internal.h"
 #include "plan.h"
 
@@ -17,6 +20,28 @@ int compare(const EwReq& r, cudaStream_t s);
 int unary(const EwReq& r, cudaStream_t s);
 int cast(const EwReq& r, cudaStream_t s);
 int fill(const EwReq& r, cudaStream_t s);
+
+// Resident blocks per SM of `kernel` at `threads` threads per block, per
+// device, queried once (cudaOccupancyMaxActiveBlocksPerMultiprocessor).
+int blocks_per_sm_cached(const void* kernel, int threads) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 1;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, kernel});
+  if (it != cache.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  cache[{dev, kernel}] = per_sm;
+  return per_sm;
+}
 }  // namespace ew
 
 int ew_run(const EwReq& r, cudaStream_t s) {

@@ -307,8 +307,12 @@ __global__ void __launch_bounds__(kEwThreads, ew_min_blocks<Op, TA, TB, TO, NIN>
 
 // -------------------------------------------------------------- EW_TILED
 // Input `a` has unit stride on dim p (an outer dim); the output is
-// contiguous along q = ndim-1. A 32x32 tile of `a` is read along p,
-// converted to TC and staged in shared memory, then written along q.
+// contiguous along q = ndim-1. Square tiles of T x T elements (T = 64 for
+// types up to 8 bytes, 32 for 16-byte ones) are read along p, converted to TC
+// and staged in shared memory (row pitch T+1: conflict-free both ways), then
+// written along q; each thread moves T*T/256 elements per tile. Blocks loop
+// over the tiles (q fastest) and load the next tile into registers while the
+// current one is written out, so loads stay in flight through the store phase.
 struct TiledArgs {
   int ndim;
   int p;
@@ -318,49 +322,108 @@ struct TiledArgs {
   int64_t bshape[kMaxCollapsed];
   int64_t bsa[kMaxCollapsed], bsb[kMaxCollapsed], bso[kMaxCollapsed];
   int64_t sa_q, sb_p, sb_q, so_p;
+  int64_t ntp, ntq, ntiles;      // tiles along p, along q, total
 };
+
+template <class TC>
+constexpr int tiled_edge() {
+  return sizeof(TC) <= 8 ? 64 : 32;
+}
+
+// Offsets of tile `ti`: its corner (p0, q0) and the batch offsets of a, b, out.
+struct TileAt {
+  int64_t p0, q0, oa, ob, oo;
+};
+MPB_D TileAt tile_at(const TiledArgs& t, int64_t ti, int T) {
+  TileAt r;
+  int64_t x = ti;
+  const int64_t bq = x % t.ntq;
+  x /= t.ntq;
+  const int64_t bp = x % t.ntp;
+  int64_t bi = x / t.ntp;
+  r.q0 = bq * T;
+  r.p0 = bp * T;
+  r.oa = r.ob = r.oo = 0;
+  for (int d = t.nb - 1; d >= 0; --d) {
+    const int64_t c = bi % t.bshape[d];
+    bi /= t.bshape[d];
+    r.oa += c * t.bsa[d];
+    r.ob += c * t.bsb[d];
+    r.oo += c * t.bso[d];
+  }
+  return r;
+}
 
 template <class Op, class TC, class TA, class TB, class TO, int NIN>
 __global__ void __launch_bounds__(256) k_ew_tiled(Op op, const TA* __restrict__ a, const TB* __restrict__ b,
                                                   TO* __restrict__ out, TiledArgs t) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
-  __shared__ __align__(16) char tile_raw[32 * 33 * sizeof(TC)];
-  TC(*tile)[33] = reinterpret_cast<TC(*)[33]>(tile_raw);
+  constexpr int T = tiled_edge<TC>();
+  constexpr int PX = T / 32;          // 32-lane chunks along a tile row
+  constexpr int EPT = T * T / 256;    // elements per thread per tile
+  __shared__ __align__(16) char tile_raw[T * (T + 1) * sizeof(TC)];
+  TC(*tile)[T + 1] = reinterpret_cast<TC(*)[T + 1]>(tile_raw);
   const int tx = threadIdx.x & 31;
   const int ty = threadIdx.x >> 5;  // 0..7
-  const int64_t q0 = (int64_t)blockIdx.x * 32;
-  const int64_t p0 = (int64_t)blockIdx.y * 32;
-  for (int64_t bi = blockIdx.z; bi < t.nbatch; bi += gridDim.z) {
-    int64_t oa = 0, ob = 0, oo = 0;
-    int64_t r = bi;
-    for (int d = t.nb - 1; d >= 0; --d) {
-      const int64_t c = r % t.bshape[d];
-      r /= t.bshape[d];
-      oa += c * t.bsa[d];
-      ob += c * t.bsb[d];
-      oo += c * t.bso[d];
-    }
-    // load a[p0+tx, q0+ty+8i] (coalesced along p)
+  TA v[EPT];
+  // a[p0 + pl, q0 + ql], coalesced along p; interior tiles skip the bounds
+  auto load = [&](const TileAt& at) {
+    const TA* ab = a + at.oa + at.p0 + tx + (at.q0 + ty) * t.sa_q;
+    const int64_t row8 = 8 * t.sa_q;
+    if (at.p0 + T <= t.dp && at.q0 + T <= t.dq) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t pp = p0 + tx, qq = q0 + ty + 8 * i;
-      if (pp < t.dp && qq < t.dq) tile[ty + 8 * i][tx] = cvt<TC>(a[oa + pp + qq * t.sa_q]);
+      for (int i = 0; i < EPT; ++i) v[i] = ab[32 * (i % PX) + (i / PX) * row8];
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) {
+        const int pl = tx + 32 * (i % PX), ql = ty + 8 * (i / PX);
+        if (at.p0 + pl < t.dp && at.q0 + ql < t.dq) v[i] = ab[32 * (i % PX) + (i / PX) * row8];
+      }
+    }
+  };
+  int64_t ti = blockIdx.x;
+  if (ti >= t.ntiles) return;
+  TileAt cur = tile_at(t, ti, T);
+  load(cur);
+  for (;;) {
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int pl = tx + 32 * (i % PX), ql = ty + 8 * (i / PX);
+      if (cur.p0 + pl < t.dp && cur.q0 + ql < t.dq) tile[ql][pl] = cvt<TC>(v[i]);
     }
     __syncthreads();
+    // the next tile's loads are in flight while this one is written out
+    const int64_t tn = ti + gridDim.x;
+    TileAt nxt{};
+    if (tn < t.ntiles) {
+      nxt = tile_at(t, tn, T);
+      load(nxt);
+    }
+    // out[p0 + pl, q0 + ql], coalesced along q
+    {
+      TO* ob = out + cur.oo + (cur.p0 + ty) * t.so_p + cur.q0 + tx;
+      const TBv* bb = reinterpret_cast<const TBv*>(b) + cur.ob + (cur.p0 + ty) * t.sb_p + (cur.q0 + tx) * t.sb_q;
+      const int64_t orow8 = 8 * t.so_p, brow8 = 8 * t.sb_p, bcol32 = 32 * t.sb_q;
+      const bool interior = cur.p0 + T <= t.dp && cur.q0 + T <= t.dq;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t pp = p0 + ty + 8 * i, qq = q0 + tx;
-      if (pp < t.dp && qq < t.dq) {
-        const TC av = tile[tx][ty + 8 * i];
-        if constexpr (NIN == 2) {
-          const TBv bv = reinterpret_cast<const TBv*>(b)[ob + pp * t.sb_p + qq * t.sb_q];
-          out[oo + pp * t.so_p + qq] = cvt<TO>(op(av, cvt<TC>(bv)));
-        } else {
-          out[oo + pp * t.so_p + qq] = cvt<TO>(op(av));
+      for (int i = 0; i < EPT; ++i) {
+        const int ql = tx + 32 * (i % PX), pl = ty + 8 * (i / PX);
+        if (interior || (cur.p0 + pl < t.dp && cur.q0 + ql < t.dq)) {
+          const TC av = tile[ql][pl];
+          TO r;
+          if constexpr (NIN == 2) {
+            r = cvt<TO>(op(av, cvt<TC>(bb[(i / PX) * brow8 + (i % PX) * bcol32])));
+          } else {
+            r = cvt<TO>(op(av));
+          }
+          ob[(i / PX) * orow8 + 32 * (i % PX)] = r;
         }
       }
     }
+    if (tn >= t.ntiles) break;
     __syncthreads();
+    ti = tn;
+    cur = nxt;
   }
 }
 

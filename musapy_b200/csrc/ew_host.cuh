@@ -153,6 +153,26 @@ inline TiledArgs tiled_args(const Geometry& g, int nin, int tx_op, int p) {
   return t;
 }
 
+// Grid for a kernel whose blocks loop over `items` work items: exactly the
+// blocks that fit on the GPU at once (256 threads each), so no block starts
+// its share after the others have finished theirs.
+int blocks_per_sm_cached(const void* kernel, int threads);  // elementwise.cu
+
+template <class K>
+unsigned resident_grid(K kernel, int64_t items) {
+  const int per_sm = blocks_per_sm_cached(reinterpret_cast<const void*>(kernel), 256);
+  int64_t blocks = (int64_t)sm_count() * per_sm;
+  if (blocks > items) blocks = items;
+  return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
+// Tile counts for an edge of `edge` elements.
+inline void tiled_count(TiledArgs& t, int edge) {
+  t.ntp = cdiv(t.dp, edge);
+  t.ntq = cdiv(t.dq, edge);
+  t.ntiles = t.ntp * t.ntq * t.nbatch;
+}
+
 template <class Op, class TC, class TA, class TB, class TO, int NIN, bool ALLOW_TILED = false>
 int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
@@ -187,13 +207,14 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
     case EW_TILED: {
       if constexpr (ALLOW_TILED) {
         TiledArgs t = tiled_args(g, NIN, pl.tiled_op, pl.tiled_p);
-        dim3 grid((unsigned)cdiv(t.dq, 32), (unsigned)cdiv(t.dp, 32),
-                  (unsigned)(t.nbatch < 65535 ? t.nbatch : 65535));
+        tiled_count(t, tiled_edge<TC>());
         if (pl.tiled_op == 0) {
-          k_ew_tiled<Op, TC, TA, TB, TO, NIN><<<grid, 256, 0, s>>>(op, a, b, out, t);
+          auto k = k_ew_tiled<Op, TC, TA, TB, TO, NIN>;
+          k<<<resident_grid(k, t.ntiles), 256, 0, s>>>(op, a, b, out, t);
         } else {
           if constexpr (NIN == 2) {
-            k_ew_tiled<Swapped<Op>, TC, TB, TA, TO, 2><<<grid, 256, 0, s>>>(Swapped<Op>{op}, b, a, out, t);
+            auto k = k_ew_tiled<Swapped<Op>, TC, TB, TA, TO, 2>;
+            k<<<resident_grid(k, t.ntiles), 256, 0, s>>>(Swapped<Op>{op}, b, a, out, t);
           }
         }
         return launch_check("ew_tiled");

@@ -246,6 +246,41 @@ def test_cast_exact(ms, oracle, src, dst):
     assert_bits_equal(got, want, f"{src}->{dst}")
 
 
+@pytest.mark.parametrize("dtype", [np.uint8, np.float16, np.float32, np.float64, np.complex128])
+@pytest.mark.parametrize("shape", [(64, 64), (1, 200), (130, 67), (3, 100, 129), (257, 33, 5)])
+def test_tiled_transposed_copies(ms, dtype, shape):
+    """contiguous() of views whose unit stride is on an outer dim (the tiled
+    shared-memory path): interior and edge tiles, batch dims, every element
+    size (16-byte elements use 32-wide tiles), bit-exact."""
+    rng = np.random.default_rng(40)
+    x = rng.standard_normal(shape)
+    if np.dtype(dtype).kind == "c":
+        x = x + 1j * rng.standard_normal(shape)
+    x = x.astype(dtype) if np.dtype(dtype).kind != "u" else rng.integers(0, 256, shape).astype(dtype)
+    xd = dev(ms, x)
+    axes = tuple(reversed(range(x.ndim)))
+    got = ms.contiguous(ms.transpose(xd)).numpy()
+    assert_bits_equal(got, np.ascontiguousarray(np.transpose(x, axes)), f"transpose {shape}")
+    if x.ndim == 3:
+        perm = (0, 2, 1)
+        got = ms.contiguous(ms.transpose(xd, perm)).numpy()
+        assert_bits_equal(got, np.ascontiguousarray(np.transpose(x, perm)), f"permute {perm} {shape}")
+
+
+def test_tiled_binary_both_operand_orders(ms, oracle):
+    """Tiled path with the transposed operand first or second and the other
+    operand a broadcast row, a broadcast column or a full array."""
+    rng = np.random.default_rng(41)
+    a = rng.standard_normal((190, 131)).astype(np.float32)
+    at = dev(ms, a).T if hasattr(dev(ms, a), "T") else ms.transpose(dev(ms, a))
+    ah = np.ascontiguousarray(a.T)
+    for other in (rng.standard_normal(190).astype(np.float32), rng.standard_normal((131, 1)).astype(np.float32),
+                  rng.standard_normal((131, 190)).astype(np.float32)):
+        od = dev(ms, other)
+        assert_bits_equal(ms.sub(at, od).numpy(), oracle.binary("sub", ah, other), "T - other")
+        assert_bits_equal(ms.sub(od, at).numpy(), oracle.binary("sub", other, ah), "other - T")
+
+
 def test_cast_strided_transposed(ms, oracle):
     x = np.random.default_rng(12).standard_normal((300, 500)).astype(np.float32)
     got = ms.transpose(dev(ms, x)).astype("bf16").numpy()
