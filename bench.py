@@ -468,7 +468,31 @@ def run_suite(args) -> None:
         del g
         return ms_per, nbytes / (ms_per * 1e-3) / 1e9
 
-    def emit(cfg, op, nbytes, fn, note="", graph=False):
+    O = None
+    if args.suite_cpu:
+        from oracle import oracle as O
+
+        O.build()
+        O.set_threads(1)
+
+    def cpu_leg(cpu):
+        """The reference CPU path (the oracle port, one thread, as the
+        reference's CPU loops are) on a bounded sample of the same op:
+        (callable, algorithmic bytes of the sample, description)."""
+        fn, nb, desc = cpu
+        fn()
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el > 1.0 or reps >= 5:
+                break
+        sec = el / reps
+        return {"value": round(nb / sec / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": desc, "ms": round(sec * 1e3, 2)}
+
+    def emit(cfg, op, nbytes, fn, note="", graph=False, cpu=None):
         t, gbs, launches = timeit(fn, nbytes)
         line = {"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1),
                 "frac": round(gbs / peak, 4), "bytes": int(nbytes), "launches": launches,
@@ -476,6 +500,8 @@ def run_suite(args) -> None:
         if graph:
             tg, gg = timeit_graph(fn, nbytes)
             line["graph"] = {"ms": round(tg, 4), "gbs": round(gg, 1), "frac": round(gg / peak, 4)}
+        if cpu is not None and O is not None:
+            line["cpu_baseline"] = cpu_leg(cpu)
         print(json.dumps(line), flush=True)
 
     cfgs = args.suite.split(",")
@@ -484,59 +510,88 @@ def run_suite(args) -> None:
         a, b = ms.from_numpy(d["a"]), ms.from_numpy(d["b"])
         c = ms.add(a, b)
         r = ms.sum(c, axis=1)
+        ch = c.numpy()
         emit("C1", "add (4096,1)+(4096,)", 4096 * 4 * 2 + 4096 * 4096 * 4, lambda: ms.add(a, b, out=c),
-             note="64 MB output: per-call host cost is a large part of ms; graph = kernels alone", graph=True)
-        emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r), graph=True)
+             note="64 MB output: per-call host cost is a large part of ms; graph = kernels alone", graph=True,
+             cpu=(lambda: O.binary("add", d["a"], d["b"]), 4096 * 4 * 2 + 4096 * 4096 * 4, "whole op"))
+        emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r), graph=True,
+             cpu=(lambda: O.reduce("sum", ch, 1), 4096 * 4096 * 4 + 4096 * 4, "whole op"))
     if "C2" in cfgs:
         d = config_inputs("C2")
         A, row, x = ms.from_numpy(d["A"]), ms.from_numpy(d["row"]), ms.from_numpy(d["x"])
+        As, rs, xs = d["A"][:512], d["row"][:512], d["x"][: 1 << 22]
         del d
         At = ms.transpose(A)
         o = ms.add(At, row)
         emit("C2", "add i64^T (8192,8192) + f64 row -> f64", 8192 * 8192 * 8 * 2 + 8192 * 8,
-             lambda: ms.add(At, row, out=o))
+             lambda: ms.add(At, row, out=o),
+             cpu=(lambda: O.binary("add", As.T, rs), 512 * 8192 * 16 + 512 * 8, "A[:512]^T + row[:512]"))
         s = ms.sin(x)
         e = ms.exp(s)
         cl = ms.clamp(e, -0.5, 0.5)
         n = 1 << 28
-        emit("C2", "sin f32 2^28", n * 8, lambda: ms.sin(x, out=s))
-        emit("C2", "exp f32 2^28", n * 8, lambda: ms.exp(s, out=e))
-        emit("C2", "clamp f32 2^28", n * 8, lambda: ms.clamp(e, -0.5, 0.5, out=cl))
+        ss = xs if O is None else O.unary("sin", xs)
+        es = ss if O is None else O.unary("exp", ss)
+        emit("C2", "sin f32 2^28", n * 8, lambda: ms.sin(x, out=s),
+             cpu=(lambda: O.unary("sin", xs), (1 << 22) * 8, "first 2^22 elements"))
+        emit("C2", "exp f32 2^28", n * 8, lambda: ms.exp(s, out=e),
+             cpu=(lambda: O.unary("exp", ss), (1 << 22) * 8, "first 2^22 elements"))
+        emit("C2", "clamp f32 2^28", n * 8, lambda: ms.clamp(e, -0.5, 0.5, out=cl),
+             cpu=(lambda: O.clamp(es, -0.5, 0.5), (1 << 22) * 8, "first 2^22 elements"))
         del A, At, o, s, e, cl, x, row
     if "C3" in cfgs:
-        x = ms.from_numpy(config_inputs("C3")["x"])
+        xh = config_inputs("C3")["x"]
+        x = ms.from_numpy(xh)
         n = 64 * 4096 * 4096 * 4
+        # CPU samples: 2 of the 64 planes for axis 2 / argmax / cumsum, 128 of
+        # the 4096 rows of every plane for axis 0 and (0, 2)
+        s2, s0 = xh[:2], np.ascontiguousarray(xh[:, :128])
+        samp = {2: (s2, 2 * 4096 * 4096 * 4, "x[:2]"), 0: (s0, 64 * 128 * 4096 * 4, "x[:, :128]"),
+                (0, 2): (s0, 64 * 128 * 4096 * 4, "x[:, :128]")}
         for axis, oelems in [(2, 64 * 4096), (0, 4096 * 4096), ((0, 2), 4096)]:
             for op in ("sum", "max", "mean"):
                 out = getattr(ms, op)(x, axis=axis)
                 f = (lambda op=op, axis=axis: getattr(ms, op)(x, axis=axis)) if isinstance(axis, tuple) else \
                     (lambda op=op, axis=axis, out=out: getattr(ms, op)(x, axis=axis, out=out))
-                emit("C3", f"{op} axis={axis}", n + oelems * 4, f)
+                sx, sb, sd = samp[axis]
+                emit("C3", f"{op} axis={axis}", n + oelems * 4, f,
+                     cpu=(lambda op=op, axis=axis, sx=sx: O.reduce(op, sx, axis), sb, sd))
         am = ms.argmax(x, axis=1)
-        emit("C3", "argmax axis=1", n + 64 * 4096 * 8, lambda: ms.argmax(x, axis=1, out=am))
+        emit("C3", "argmax axis=1", n + 64 * 4096 * 8, lambda: ms.argmax(x, axis=1, out=am),
+             cpu=(lambda: O.reduce("argmax", s2, 1), 2 * 4096 * 4096 * 4, "x[:2]"))
         cs = ms.cumsum(x, axis=-1)
-        emit("C3", "cumsum axis=-1", 2 * n, lambda: ms.cumsum(x, axis=-1, out=cs))
-        del x, cs, am
+        emit("C3", "cumsum axis=-1", 2 * n, lambda: ms.cumsum(x, axis=-1, out=cs),
+             cpu=(lambda: O.cumsum(s2, -1), 2 * 2 * 4096 * 4096 * 4, "x[:2] (running-sum form)"))
+        del x, cs, am, xh, s2, s0
     if "C4" in cfgs:
         d = config_inputs("C4")
         n = 1 << 30
         x = ms.from_numpy(d["x"])
+        m = 1 << 22
+        xs_, as_, bs_, z1s, z2s = d["x"][:m], d["a"][:m], d["b"][:m], d["z1"][:m], d["z2"][:m]
+        xbs = xs_ if O is None else O.cast(xs_, O.BF16)
         xb = x.astype("bf16")
         back = xb.astype("f32")
-        emit("C4", "astype f32->bf16 2^30", n * 6, lambda: ms.astype(x, "bf16", out=xb))
-        emit("C4", "astype bf16->f32 2^30", n * 6, lambda: ms.astype(xb, "f32", out=back))
+        emit("C4", "astype f32->bf16 2^30", n * 6, lambda: ms.astype(x, "bf16", out=xb),
+             cpu=(lambda: O.cast(xs_, O.BF16), m * 6, "first 2^22 elements"))
+        emit("C4", "astype bf16->f32 2^30", n * 6, lambda: ms.astype(xb, "f32", out=back),
+             cpu=(lambda: O.cast(xbs, O.F32), m * 6, "first 2^22 elements"))
         del x, xb, back
         a, b = ms.from_numpy(d["a"]), ms.from_numpy(d["b"])
         p = ms.pow(a, b)
-        emit("C4", "pow f16 2^30", n * 6, lambda: ms.pow(a, b, out=p))
+        emit("C4", "pow f16 2^30", n * 6, lambda: ms.pow(a, b, out=p),
+             cpu=(lambda: O.binary("pow", as_, bs_), m * 6, "first 2^22 elements"))
         del p
         lt = ms.lt(a, b)
-        emit("C4", "lt f16 -> bool 2^30", n * 5, lambda: ms.lt(a, b, out=lt))
-        emit("C4", "eq f16 -> bool 2^30", n * 5, lambda: ms.eq(a, b, out=lt))
+        emit("C4", "lt f16 -> bool 2^30", n * 5, lambda: ms.lt(a, b, out=lt),
+             cpu=(lambda: O.compare("lt", as_, bs_), m * 5, "first 2^22 elements"))
+        emit("C4", "eq f16 -> bool 2^30", n * 5, lambda: ms.eq(a, b, out=lt),
+             cpu=(lambda: O.compare("eq", as_, bs_), m * 5, "first 2^22 elements"))
         del a, b, lt
         z1, z2 = ms.from_numpy(d["z1"]), ms.from_numpy(d["z2"])
         z = ms.mul(z1, z2)
-        emit("C4", "mul c64 2^27", (1 << 27) * 24, lambda: ms.mul(z1, z2, out=z))
+        emit("C4", "mul c64 2^27", (1 << 27) * 24, lambda: ms.mul(z1, z2, out=z),
+             cpu=(lambda: O.binary("mul", z1s, z2s), m * 24, "first 2^22 elements"))
         del z1, z2, z, d
     if "NEXT" in cfgs:
         # the survey's "next" rows: contiguous copies of views, creation
@@ -590,6 +645,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--suite", default="", help="comma list of C1..C4, NEXT: time every op of those configs")
+    ap.add_argument("--suite-cpu", action="store_true",
+                    help="with --suite: also time the reference CPU path (oracle port, 1 thread) on a sample")
     args = ap.parse_args()
     if args.suite:
         run_suite(args)

@@ -183,6 +183,24 @@ int mpb_linspace(void* out, int dtype, int64_t n, double start, double stop, mpb
  * (init.mu:121-134); every dtype is accepted. */
 int mpb_eye(void* out, int dtype, int64_t rows, int64_t cols, int64_t k, mpb_stream_t stream);
 
+/* --------------------------------------------------- host <-> device copies */
+
+/* Copies `bytes` from pageable (or any) host memory to device memory `dst`
+ * on `stream`, through a ring of pinned staging slots with the host-side
+ * copies spread over a few threads and overlapped with the DMA of the
+ * previous chunk. Returns once the host source has been read completely (it
+ * may be reused at once); the device copy completes in stream order. Replaces
+ * the list-based host transfer of ms.array (rust/musapy-python/src/ops.rs:
+ * 354-625) and the plain musaMemcpy behind it (musa_ffi.rs). The device is the
+ * current CUDA device. */
+int mpb_copy_h2d(void* dst, const void* src, size_t bytes, mpb_stream_t stream);
+
+/* Copies `bytes` of device memory `src` to host memory `dst` after the work
+ * already queued on `stream`, and returns when `dst` holds the data. Same
+ * staging ring as mpb_copy_h2d, the DMA of chunk k+4 overlapping the host
+ * copy of chunk k. Replaces Array.tolist's transfer (array.rs:451-488). */
+int mpb_copy_d2h(void* dst, const void* src, size_t bytes, mpb_stream_t stream);
+
 /* ---------------------------------------------------- axis-0 sharding (new) */
 
 /* Device combine of per-rank argmax/argmin records (MPB_R_ARG*_REC output,

@@ -106,6 +106,10 @@ def _load() -> ctypes.CDLL:
     L.mpb_linspace.argtypes = [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_double, c_vp]
     L.mpb_eye.restype = ctypes.c_int
     L.mpb_eye.argtypes = [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, c_vp]
+    L.mpb_copy_h2d.restype = ctypes.c_int
+    L.mpb_copy_h2d.argtypes = [c_vp, c_vp, ctypes.c_size_t, c_vp]
+    L.mpb_copy_d2h.restype = ctypes.c_int
+    L.mpb_copy_d2h.argtypes = [c_vp, c_vp, ctypes.c_size_t, c_vp]
     return L
 
 

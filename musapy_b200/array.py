@@ -6,6 +6,7 @@ ordered); views share the buffer and only change the layout.
 from __future__ import annotations
 
 import builtins
+import mmap
 import numbers
 from typing import Iterable, Sequence
 
@@ -18,6 +19,9 @@ from . import streams as _streams
 
 _DEFAULT_DEVICE = [0]
 _DEFAULT_DTYPE = [_dt.float32]
+# host transfers from this size on go through the pinned staging ring
+# (mpb_copy_h2d / mpb_copy_d2h); smaller ones through torch's copy
+_STAGED_COPY_BYTES = 1 << 20
 
 
 class Device:
@@ -222,8 +226,15 @@ class Array:
         if n == 0:
             return np.zeros(a._shape, dtype=_dt.to_numpy(a._dtype))
         start = a._offset * a._dtype.itemsize
-        _streams.launch("numpy", a._dev, a)
-        host = a._buf.narrow(0, start, n).cpu().numpy()
+        handle = _streams.launch("numpy", a._dev, a)
+        if n >= _STAGED_COPY_BYTES:
+            host = _host_buffer(n)
+            from ._lib import LIB, check
+
+            with torch.cuda.device(a._dev):
+                check(LIB.mpb_copy_d2h(host.ctypes.data, a._buf.data_ptr() + start, n, handle), "numpy")
+        else:
+            host = a._buf.narrow(0, start, n).cpu().numpy()
         return host.view(_dt.to_numpy(a._dtype)).reshape(a._shape)
 
     def tolist(self):
@@ -385,6 +396,21 @@ def _has_complex(data) -> bool:
     return False
 
 
+def _host_buffer(n: int) -> np.ndarray:
+    """A fresh host byte array for a device -> host copy. Large ones are an
+    anonymous mapping advised for transparent huge pages: the copy then
+    faults in 2 MiB pages instead of 4 KiB ones, which is most of the cost of
+    filling fresh memory."""
+    if n >= (64 << 20) and hasattr(mmap, "MADV_HUGEPAGE"):
+        mm = mmap.mmap(-1, n, flags=mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS)
+        try:
+            mm.madvise(mmap.MADV_HUGEPAGE)
+        except OSError:
+            pass
+        return np.frombuffer(mm, dtype=np.uint8)
+    return np.empty(n, dtype=np.uint8)
+
+
 def from_numpy(arr: np.ndarray, device=None, dtype=None) -> Array:
     """Copy a numpy array to the device (dtype kept unless given)."""
     arr = np.asarray(arr)
@@ -396,9 +422,14 @@ def from_numpy(arr: np.ndarray, device=None, dtype=None) -> Array:
     out = empty(arr.shape, d, device)
     n = arr.nbytes
     if n:
-        src = torch.from_numpy(arr.reshape(-1).view(np.uint8))
-        _streams.launch("from_numpy", out._dev, out)
-        out._buf[:n].copy_(src)
+        handle = _streams.launch("from_numpy", out._dev, out)
+        if n >= _STAGED_COPY_BYTES:
+            from ._lib import LIB, check
+
+            with torch.cuda.device(out._dev):
+                check(LIB.mpb_copy_h2d(out._buf.data_ptr(), arr.ctypes.data, n, handle), "from_numpy")
+        else:
+            out._buf[:n].copy_(torch.from_numpy(arr.reshape(-1).view(np.uint8)))
     return out
 
 

@@ -105,3 +105,44 @@ def test_default_stream_ops_follow_torch_current_stream(ms):
         assert ms.streams.current_stream(0).cuda_stream == side.cuda_stream
     torch.cuda.synchronize()
     assert a.tolist() == [0.0, 1.0, 2.0, 3.0]
+
+
+@pytest.mark.parametrize("nbytes", [(1 << 20) - 1, 1 << 20, (1 << 20) + 3, (100 << 20) + 7, (300 << 20) + 5])
+def test_staged_host_transfers_round_trip(ms, nbytes):
+    """from_numpy / numpy() through the pinned staging ring (sizes below,
+    at and above the threshold, not multiples of 16, larger than the ring)."""
+    rng = np.random.default_rng(nbytes % 1000)
+    host = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    d = ms.from_numpy(host)
+    back = d.numpy()
+    assert back.dtype == np.uint8 and np.array_equal(back, host)
+    # a device-side op in between: the copy-out sees its result
+    f = rng.standard_normal(nbytes // 8).astype(np.float64)
+    fd = ms.from_numpy(f)
+    neg = ms.neg(fd).numpy()
+    assert np.array_equal(neg, -f)
+
+
+def test_staged_copy_waits_for_other_stream(ms):
+    n = 1 << 24
+    s1 = ms.Stream("cuda:0")
+    with ms.stream(s1):
+        x = ms.zeros((n,), dtype="f32")
+        one = ms.ones((n,), dtype="f32")
+        y = ms.empty((n,), dtype="f32")
+        for _ in range(30):
+            ms.add(x, one, out=y)
+            x, y = y, x
+    # copied out on the default stream: waits for s1's chain
+    h = x.numpy()
+    assert h.min() == 30.0 and h.max() == 30.0
+
+
+def test_from_numpy_views_and_complex(ms):
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((1024, 768)) + 1j * rng.standard_normal((1024, 768))
+    v = a[::2, ::-3]
+    d = ms.from_numpy(v)
+    assert np.array_equal(d.numpy(), v)
+    z = ms.from_numpy(np.float32(2.5))
+    assert z.shape == () and z.item() == 2.5
