@@ -116,9 +116,13 @@ def _load() -> ctypes.CDLL:
 LIB = _load()
 
 
+_I64_TYPES = [ctypes.c_int64 * max(1, n) for n in range(33)]
+
+
 def i64arr(vals) -> ctypes.Array:
-    vals = list(vals)
-    return (ctypes.c_int64 * max(1, len(vals)))(*vals)
+    n = len(vals)
+    t = _I64_TYPES[n] if n <= 32 else ctypes.c_int64 * n
+    return t(*vals)
 
 
 def last_error() -> str:

@@ -158,9 +158,16 @@ def from_torch(td: torch.dtype) -> Dtype:
 def promote(a: Dtype, b: Dtype, all_gpu: bool = True) -> Dtype:
     """Result dtype of a binary op (dtype.rs:302-338); all_gpu selects the
     narrow-first rule musapy uses when every input lives on the device."""
-    from ._lib import LIB
+    key = (a.code, b.code, bool(all_gpu))
+    d = _PROMOTE_CACHE.get(key)
+    if d is None:
+        from ._lib import LIB
 
-    code = LIB.mpb_promote(a.code, b.code, 1 if all_gpu else 0)
-    if code < 0:
-        raise errors.DtypeError(f"cannot promote {a} with {b}")
-    return BY_CODE[code]
+        code = LIB.mpb_promote(a.code, b.code, 1 if all_gpu else 0)
+        if code < 0:
+            raise errors.DtypeError(f"cannot promote {a} with {b}")
+        d = _PROMOTE_CACHE[key] = BY_CODE[code]
+    return d
+
+
+_PROMOTE_CACHE: dict = {}

@@ -73,19 +73,41 @@ def _coerce_pair(a, b):
 
 
 def _broadcast_shape(a: Array, b: Array) -> tuple:
-    out = i64arr([0] * builtins.max(a.ndim, b.ndim, 1))
-    n = LIB.mpb_broadcast_shape(a.ndim, i64arr(a.shape), b.ndim, i64arr(b.shape), out)
-    if n < 0:
-        raise errors.ShapeError(f"broadcast: incompatible shapes {list(a.shape)} and {list(b.shape)}")
-    return tuple(out[:n])
+    """broadcast_shape (broadcast.rs:24-55): align from the right; extents
+    must match or be 1. (Same rule as mpb_broadcast_shape, without a library
+    call on the per-op path; the two are tested against each other.)"""
+    sa, sb = a._shape, b._shape
+    if sa == sb:
+        return sa
+    na, nb = len(sa), len(sb)
+    n = na if na > nb else nb
+    out = []
+    for i in range(n):
+        da = sa[i - n + na] if i >= n - na else 1
+        db = sb[i - n + nb] if i >= n - nb else 1
+        if da == db or db == 1:
+            out.append(da)
+        elif da == 1:
+            out.append(db)
+        else:
+            raise errors.ShapeError(f"broadcast: incompatible shapes {list(sa)} and {list(sb)}")
+    return tuple(out)
 
 
-def _bstrides(a: Array, shape) -> list:
-    if a.shape == tuple(shape):
-        return list(a.strides)
-    out = i64arr([0] * builtins.max(1, len(shape)))
-    LIB.mpb_broadcast_strides(a.ndim, i64arr(a.shape), i64arr(a.strides), len(shape), i64arr(shape), out)
-    return list(out[: len(shape)])
+def _bstrides(a: Array, shape) -> tuple:
+    """broadcast_strides (broadcast.rs:57-92): the view's strides on `shape`,
+    0 where a dim is added or stretched from 1."""
+    if a._shape == shape:
+        return a._strides
+    n, na = len(shape), len(a._shape)
+    st = []
+    for i in range(n):
+        j = i - (n - na)
+        if j < 0 or (a._shape[j] == 1 and shape[i] != 1):
+            st.append(0)
+        else:
+            st.append(a._strides[j])
+    return tuple(st)
 
 
 def _check_out(out: Array, shape, dtype: _dt.Dtype, dev: int, name: str) -> None:

@@ -125,3 +125,46 @@ def test_creation_errors(oracle, case):
     src, kind, args = case
     with pytest.raises(ValueError):
         getattr(oracle, kind)(*args)
+
+
+def _cpu_view(shape, strides):
+    import sys
+
+    import torch
+
+    A = sys.modules["musapy_b200.array"].Array
+    from musapy_b200 import float32
+
+    return A(torch.empty(16, dtype=torch.uint8), tuple(shape), tuple(strides), 0, float32, 0)
+
+
+def test_python_broadcast_helpers_match_library():
+    """ops.py's per-op broadcast shape/strides against the library's
+    restatement (which the reference's broadcast.rs vectors pin), on those
+    vectors and on random shapes."""
+    import random
+
+    from musapy_b200 import errors, ops
+    from musapy_b200._lib import LIB, i64arr
+
+    cases = [(a, b) for a, b, _, _ in K.BROADCAST_SHAPE]
+    rnd = random.Random(7)
+    for _ in range(400):
+        na, nb = rnd.randint(0, 5), rnd.randint(0, 5)
+        a = [rnd.choice([1, 1, 2, 3, 5]) for _ in range(na)]
+        b = [rnd.choice([1, 1, 2, 3, 5]) for _ in range(nb)]
+        cases.append((a, b))
+    for a, b in cases:
+        out = i64arr([0] * max(len(a), len(b), 1))
+        n = LIB.mpb_broadcast_shape(len(a), i64arr(a), len(b), i64arr(b), out)
+        va, vb = _cpu_view(a, [3 + i for i in range(len(a))]), _cpu_view(b, [7 * i - 2 for i in range(len(b))])
+        if n < 0:
+            with pytest.raises(errors.ShapeError):
+                ops._broadcast_shape(va, vb)
+            continue
+        shape = tuple(out[:n])
+        assert ops._broadcast_shape(va, vb) == shape, (a, b)
+        for v in (va, vb):
+            st = i64arr([0] * max(1, len(shape)))
+            LIB.mpb_broadcast_strides(v.ndim, i64arr(v.shape), i64arr(v.strides), len(shape), i64arr(shape), st)
+            assert list(ops._bstrides(v, shape)) == list(st[: len(shape)]), (v.shape, shape)
