@@ -383,8 +383,10 @@ def run_b200(args) -> None:
 
 
 # ------------------------------------------------------- per-config suite
-def config_inputs(name: str):
-    """Seeded inputs of BASELINE configs 1-4 (numpy PCG64; seeds 0, 2, 1, 4)."""
+def config_inputs(name: str, scale: int = 1):
+    """Seeded inputs of BASELINE configs 1-4 (numpy PCG64; seeds 0, 2, 1, 4).
+    `scale` > 1 divides the large extents (C2's chain, C3's leading dim, C4's
+    lengths) for small profiling runs; 1 is the benchmark's size."""
     import numpy as np
 
     if name == "C1":
@@ -396,18 +398,19 @@ def config_inputs(name: str):
         rng = np.random.default_rng(2)
         A = rng.integers(-1000, 1001, (8192, 8192), dtype=np.int64)
         row = rng.standard_normal(8192)
-        x = rng.standard_normal(1 << 28, dtype=np.float32)
+        x = rng.standard_normal((1 << 28) // scale, dtype=np.float32)
         return {"A": A, "row": row, "x": x}
     if name == "C3":
         rng = np.random.default_rng(1)
-        return {"x": rng.standard_normal((64, 4096, 4096), dtype=np.float32)}
+        return {"x": rng.standard_normal((64 // scale, 4096, 4096), dtype=np.float32)}
     if name == "C4":
         rng = np.random.default_rng(4)
-        x = rng.standard_normal(1 << 30, dtype=np.float32)
-        a = (0.1 + 3.9 * rng.random(1 << 30, dtype=np.float32)).astype(np.float16)
-        b = (-2 + 4 * rng.random(1 << 30, dtype=np.float32)).astype(np.float16)
-        re, im = rng.standard_normal((2, 1 << 27), dtype=np.float32)
-        re2, im2 = rng.standard_normal((2, 1 << 27), dtype=np.float32)
+        n, m = (1 << 30) // scale, (1 << 27) // scale
+        x = rng.standard_normal(n, dtype=np.float32)
+        a = (0.1 + 3.9 * rng.random(n, dtype=np.float32)).astype(np.float16)
+        b = (-2 + 4 * rng.random(n, dtype=np.float32)).astype(np.float16)
+        re, im = rng.standard_normal((2, m), dtype=np.float32)
+        re2, im2 = rng.standard_normal((2, m), dtype=np.float32)
         return {"x": x, "a": a, "b": b, "z1": (re + 1j * im).astype(np.complex64),
                 "z2": (re2 + 1j * im2).astype(np.complex64)}
     raise KeyError(name)
@@ -496,7 +499,7 @@ def run_suite(args) -> None:
         t, gbs, launches = timeit(fn, nbytes)
         line = {"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1),
                 "frac": round(gbs / peak, 4), "bytes": int(nbytes), "launches": launches,
-                "peak": peak, "peak_kind": peak_kind, "note": note}
+                "peak": peak, "peak_kind": peak_kind, "note": note, "scale": args.scale}
         if graph:
             tg, gg = timeit_graph(fn, nbytes)
             line["graph"] = {"ms": round(tg, 4), "gbs": round(gg, 1), "frac": round(gg / peak, 4)}
@@ -517,7 +520,7 @@ def run_suite(args) -> None:
         emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r), graph=True,
              cpu=(lambda: O.reduce("sum", ch, 1), 4096 * 4096 * 4 + 4096 * 4, "whole op"))
     if "C2" in cfgs:
-        d = config_inputs("C2")
+        d = config_inputs("C2", args.scale)
         A, row, x = ms.from_numpy(d["A"]), ms.from_numpy(d["row"]), ms.from_numpy(d["x"])
         As, rs, xs = d["A"][:512], d["row"][:512], d["x"][: 1 << 22]
         del d
@@ -529,7 +532,7 @@ def run_suite(args) -> None:
         s = ms.sin(x)
         e = ms.exp(s)
         cl = ms.clamp(e, -0.5, 0.5)
-        n = 1 << 28
+        n = x.size
         ss = xs if O is None else O.unary("sin", xs)
         es = ss if O is None else O.unary("exp", ss)
         emit("C2", "sin f32 2^28", n * 8, lambda: ms.sin(x, out=s),
@@ -540,15 +543,15 @@ def run_suite(args) -> None:
              cpu=(lambda: O.clamp(es, -0.5, 0.5), (1 << 22) * 8, "first 2^22 elements"))
         del A, At, o, s, e, cl, x, row
     if "C3" in cfgs:
-        xh = config_inputs("C3")["x"]
+        xh = config_inputs("C3", args.scale)["x"]
         x = ms.from_numpy(xh)
-        n = 64 * 4096 * 4096 * 4
+        n = xh.nbytes
+        P = xh.shape[0]
         # CPU samples: 2 of the 64 planes for axis 2 / argmax / cumsum, 128 of
         # the 4096 rows of every plane for axis 0 and (0, 2)
         s2, s0 = xh[:2], np.ascontiguousarray(xh[:, :128])
-        samp = {2: (s2, 2 * 4096 * 4096 * 4, "x[:2]"), 0: (s0, 64 * 128 * 4096 * 4, "x[:, :128]"),
-                (0, 2): (s0, 64 * 128 * 4096 * 4, "x[:, :128]")}
-        for axis, oelems in [(2, 64 * 4096), (0, 4096 * 4096), ((0, 2), 4096)]:
+        samp = {2: (s2, s2.nbytes, "x[:2]"), 0: (s0, s0.nbytes, "x[:, :128]"), (0, 2): (s0, s0.nbytes, "x[:, :128]")}
+        for axis, oelems in [(2, P * 4096), (0, 4096 * 4096), ((0, 2), 4096)]:
             for op in ("sum", "max", "mean"):
                 out = getattr(ms, op)(x, axis=axis)
                 f = (lambda op=op, axis=axis: getattr(ms, op)(x, axis=axis)) if isinstance(axis, tuple) else \
@@ -557,15 +560,15 @@ def run_suite(args) -> None:
                 emit("C3", f"{op} axis={axis}", n + oelems * 4, f,
                      cpu=(lambda op=op, axis=axis, sx=sx: O.reduce(op, sx, axis), sb, sd))
         am = ms.argmax(x, axis=1)
-        emit("C3", "argmax axis=1", n + 64 * 4096 * 8, lambda: ms.argmax(x, axis=1, out=am),
-             cpu=(lambda: O.reduce("argmax", s2, 1), 2 * 4096 * 4096 * 4, "x[:2]"))
+        emit("C3", "argmax axis=1", n + P * 4096 * 8, lambda: ms.argmax(x, axis=1, out=am),
+             cpu=(lambda: O.reduce("argmax", s2, 1), s2.nbytes + 2 * 4096 * 8, "x[:2]"))
         cs = ms.cumsum(x, axis=-1)
         emit("C3", "cumsum axis=-1", 2 * n, lambda: ms.cumsum(x, axis=-1, out=cs),
-             cpu=(lambda: O.cumsum(s2, -1), 2 * 2 * 4096 * 4096 * 4, "x[:2] (running-sum form)"))
+             cpu=(lambda: O.cumsum(s2, -1), 2 * s2.nbytes, "x[:2] (running-sum form)"))
         del x, cs, am, xh, s2, s0
     if "C4" in cfgs:
-        d = config_inputs("C4")
-        n = 1 << 30
+        d = config_inputs("C4", args.scale)
+        n = d["x"].size
         x = ms.from_numpy(d["x"])
         m = 1 << 22
         xs_, as_, bs_, z1s, z2s = d["x"][:m], d["a"][:m], d["b"][:m], d["z1"][:m], d["z2"][:m]
@@ -590,7 +593,7 @@ def run_suite(args) -> None:
         del a, b, lt
         z1, z2 = ms.from_numpy(d["z1"]), ms.from_numpy(d["z2"])
         z = ms.mul(z1, z2)
-        emit("C4", "mul c64 2^27", (1 << 27) * 24, lambda: ms.mul(z1, z2, out=z),
+        emit("C4", "mul c64 2^27", d["z1"].size * 24, lambda: ms.mul(z1, z2, out=z),
              cpu=(lambda: O.binary("mul", z1s, z2s), m * 24, "first 2^22 elements"))
         del z1, z2, z, d
     if "NEXT" in cfgs:
@@ -645,6 +648,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--suite", default="", help="comma list of C1..C4, NEXT: time every op of those configs")
+    ap.add_argument("--scale", type=int, default=1,
+                    help="with --suite: divide the large extents of C2-C4 by this power of two (profiling runs)")
     ap.add_argument("--suite-cpu", action="store_true",
                     help="with --suite: also time the reference CPU path (oracle port, 1 thread) on a sample")
     args = ap.parse_args()

@@ -323,6 +323,7 @@ struct TiledArgs {
   int64_t bsa[kMaxCollapsed], bsb[kMaxCollapsed], bso[kMaxCollapsed];
   int64_t sa_q, sb_p, sb_q, so_p;
   int64_t ntp, ntq, ntiles;      // tiles along p, along q, total
+  FastDiv fd_ntq, fd_ntp;        // for tile indices below 2^32
 };
 
 template <class TC>
@@ -336,11 +337,21 @@ struct TileAt {
 };
 MPB_D TileAt tile_at(const TiledArgs& t, int64_t ti, int T) {
   TileAt r;
-  int64_t x = ti;
-  const int64_t bq = x % t.ntq;
-  x /= t.ntq;
-  const int64_t bp = x % t.ntp;
-  int64_t bi = x / t.ntp;
+  int64_t bq, bp, bi;
+  if (t.ntiles < 0xffffffffLL) {  // magic-number division (a 64-bit divide is ~100 instructions)
+    uint32_t x, q, rem;
+    t.fd_ntq.divmod((uint32_t)ti, x, rem);
+    bq = rem;
+    t.fd_ntp.divmod(x, q, rem);
+    bp = rem;
+    bi = q;
+  } else {
+    int64_t x = ti;
+    bq = x % t.ntq;
+    x /= t.ntq;
+    bp = x % t.ntp;
+    bi = x / t.ntp;
+  }
   r.q0 = bq * T;
   r.p0 = bp * T;
   r.oa = r.ob = r.oo = 0;

@@ -171,6 +171,8 @@ inline void tiled_count(TiledArgs& t, int edge) {
   t.ntp = cdiv(t.dp, edge);
   t.ntq = cdiv(t.dq, edge);
   t.ntiles = t.ntp * t.ntq * t.nbatch;
+  t.fd_ntq = FastDiv((uint32_t)(t.ntq < 0xffffffffLL ? t.ntq : 1));
+  t.fd_ntp = FastDiv((uint32_t)(t.ntp < 0xffffffffLL ? t.ntp : 1));
 }
 
 template <class Op, class TC, class TA, class TB, class TO, int NIN, bool ALLOW_TILED = false>

@@ -264,6 +264,7 @@ struct RedDev {
 };
 
 MPB_D int64_t kept_off(const RedDev& g, int64_t o) {
+  if (g.K <= 1) return g.K == 1 ? o * g.kst[0] : 0;  // o < ks[0]: no division
   int64_t off = 0;
   for (int d = g.K - 1; d >= 0; --d) {
     const int64_t c = o % g.ks[d];
