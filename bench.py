@@ -355,6 +355,9 @@ def run_b200(args) -> None:
         cpu = cpu_sample(args.sample_rows, cols, 1, 1, 0)
 
     if world > 1:
+        for ex in list(sh._EXCHANGES.values()):
+            ex.check()  # a peer-exchange wait that gave up invalidates the run
+        sh.close_exchanges()
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:

@@ -215,6 +215,37 @@ int mpb_shard_arg_combine(const int64_t* records, int nranks, const int64_t* ran
 int mpb_shard_sum_finalize(const double* total, double count, int out_dtype, void* sum_out, void* mean_out,
                            mpb_stream_t stream);
 
+/* ------------------------------------------- peer record exchange (new) */
+
+/* Record exchange over NVLink peer memory between the ranks of one node, the
+ * last step of a sharded full reduction. No counterpart in musapy, which has
+ * no multi-GPU path. Each rank allocates one exchange buffer
+ * (mpb_peer_alloc: cudaMalloc of mpb_peer_buffer_bytes() bytes, zeroed, plus
+ * its CUDA IPC handle of mpb_peer_handle_bytes() bytes), the handles are
+ * exchanged out of band, and each rank opens the others (mpb_peer_open). */
+size_t mpb_peer_buffer_bytes(void);
+size_t mpb_peer_handle_bytes(void);
+int mpb_peer_alloc(void** buf, void* ipc_handle);
+int mpb_peer_open(const void* ipc_handle, void** peer_buf);
+int mpb_peer_close(void* peer_buf);
+int mpb_peer_free(void* buf);
+
+/* Exchange number `seq` (1, 2, ... the same sequence on every rank): stores
+ * this rank's `rec_bytes` (16 or 32) record into every rank's buffer
+ * (peers[r] is rank r's buffer as mapped here, peers[rank] the local one),
+ * then waits until all `world` records of this exchange have arrived and
+ * writes them to `out` in rank order (world x rec_bytes, 16-byte aligned).
+ * Waits are bounded (~2 s): on expiry *status (device int) becomes
+ * MPB_ERR_TIMEOUT and the kernel returns. At most 16 ranks. */
+int mpb_peer_allgather(const void* rec, int rec_bytes, void* const* peers, int rank, int world, uint64_t seq,
+                       void* out, int* status, mpb_stream_t stream);
+
+/* Sum of `world` f64 partials (stride_bytes apart) in rank order, then sum
+ * and mean (over `count` elements) in MPB_F32 or MPB_F64. No counterpart in
+ * musapy. */
+int mpb_shard_sum_parts_finalize(const double* parts, int stride_bytes, int world, double count, int out_dtype,
+                                 void* sum_out, void* mean_out, mpb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -110,6 +110,22 @@ def _load() -> ctypes.CDLL:
     L.mpb_copy_h2d.argtypes = [c_vp, c_vp, ctypes.c_size_t, c_vp]
     L.mpb_copy_d2h.restype = ctypes.c_int
     L.mpb_copy_d2h.argtypes = [c_vp, c_vp, ctypes.c_size_t, c_vp]
+    L.mpb_peer_buffer_bytes.restype = ctypes.c_size_t
+    L.mpb_peer_handle_bytes.restype = ctypes.c_size_t
+    L.mpb_peer_alloc.restype = ctypes.c_int
+    L.mpb_peer_alloc.argtypes = [ctypes.POINTER(c_vp), c_vp]
+    L.mpb_peer_open.restype = ctypes.c_int
+    L.mpb_peer_open.argtypes = [c_vp, ctypes.POINTER(c_vp)]
+    L.mpb_peer_close.restype = ctypes.c_int
+    L.mpb_peer_close.argtypes = [c_vp]
+    L.mpb_peer_free.restype = ctypes.c_int
+    L.mpb_peer_free.argtypes = [c_vp]
+    L.mpb_peer_allgather.restype = ctypes.c_int
+    L.mpb_peer_allgather.argtypes = [c_vp, ctypes.c_int, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_uint64, c_vp, c_vp, c_vp]
+    L.mpb_shard_sum_parts_finalize.restype = ctypes.c_int
+    L.mpb_shard_sum_parts_finalize.argtypes = [c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int,
+                                               c_vp, c_vp, c_vp]
     return L
 
 

@@ -6,10 +6,13 @@ of a global array; broadcast operands (a row vector) are replicated.
 
 * elementwise ops run on each shard independently (no communication);
 * reductions over non-leading axes stay local;
-* full reductions reduce the local shard on the GPU, move one tiny record per
-  rank with ONE collective over NVLink (NCCL all_reduce for sum/mean, NCCL
-  all_gather of (value, index) records for argmax/argmin), and finish on the
-  device with a one-thread combine kernel, so no host round trip is needed.
+* full reductions reduce the local shard on the GPU, move one 16-byte record
+  per rank over NVLink with ONE exchange - by default a peer-memory all-gather
+  kernel (PeerExchange: P2P stores into every rank's IPC-shared buffer and
+  bounded flag waits), or NCCL (all_reduce for sum/mean, all_gather for
+  argmax/argmin) with MUSAPY_B200_SHARD_COLLECTIVE=nccl - and finish on the
+  device with a one-thread combine in rank order, so no host round trip is
+  needed.
 
 The process group is torch.distributed's (backend "nccl" on GPUs, "gloo" in
 the CPU tests of the combine logic).
@@ -56,6 +59,90 @@ class ShardedArray:
         return n
 
 
+class PeerExchange:
+    """Small-record all-gather over NVLink peer memory (mpb_peer_allgather):
+    one exchange buffer per rank shared by CUDA IPC, one kernel per exchange,
+    sequence numbers kept identical on all ranks by calling exchanges in the
+    same order everywhere (as collectives already must be)."""
+
+    def __init__(self, dev: int, group=None) -> None:
+        import ctypes
+
+        self.dev, self.group = dev, group
+        self.world, self.rank = _world(group)
+        self.seq = 0
+        self._buf = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(int(LIB.mpb_peer_handle_bytes()))
+        with torch.cuda.device(dev):
+            check(LIB.mpb_peer_alloc(ctypes.byref(self._buf), handle), "peer exchange")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        ptrs = []
+        self._opened = []
+        with torch.cuda.device(dev):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._buf.value)
+                    continue
+                p = ctypes.c_void_p()
+                hb = ctypes.create_string_buffer(h, len(h))
+                check(LIB.mpb_peer_open(hb, ctypes.byref(p)), "peer exchange")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+        self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+
+    def allgather(self, rec: torch.Tensor, out: torch.Tensor, stream: int) -> None:
+        """rec: 16 or 32 bytes on this rank's device; out: world x that, in rank order."""
+        self.seq += 1
+        check(LIB.mpb_peer_allgather(rec.data_ptr(), rec.nbytes, self._ptrs, self.rank, self.world, self.seq,
+                                     out.data_ptr(), self.status.data_ptr(), stream), "peer exchange")
+
+    def check(self) -> None:
+        """Raise if any exchange gave up waiting for a rank (synchronises)."""
+        if int(self.status.item()) != 0:
+            raise errors.StreamError(f"peer exchange on cuda:{self.dev}: a rank did not arrive within the wait limit")
+
+    def close(self) -> None:
+        """Collective: every rank synchronises, meets at a barrier (so no
+        exchange kernel is still writing into anyone's buffer), then unmaps."""
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.dev):
+            for p in self._opened:
+                LIB.mpb_peer_close(p)
+            self._opened = []
+        dist.barrier(group=self.group)
+
+
+_EXCHANGES: dict = {}
+
+
+def peer_exchange(dev: int, group=None) -> PeerExchange | None:
+    """The node's peer exchange for (dev, group), created on first use by all
+    ranks together; None when there is a single rank or when the transport is
+    NCCL (MUSAPY_B200_SHARD_COLLECTIVE=nccl)."""
+    import os
+
+    world, _ = _world(group)
+    if world <= 1 or os.environ.get("MUSAPY_B200_SHARD_COLLECTIVE", "peer") == "nccl":
+        return None
+    if dist.get_backend(group) != "nccl":  # CPU process groups (gloo) have no device buffers
+        return None
+    key = (dev, id(group))
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = PeerExchange(dev, group)
+    return ex
+
+
+def close_exchanges() -> None:
+    """Collective teardown of every peer exchange (call on all ranks before
+    destroy_process_group)."""
+    for key in list(_EXCHANGES):
+        _EXCHANGES.pop(key).close()
+
+
 def _world(group) -> tuple[int, int]:
     if dist.is_available() and dist.is_initialized():
         return dist.get_world_size(group), dist.get_rank(group)
@@ -76,10 +163,12 @@ def sum_axis(x: ShardedArray, axis: int, out: Array | None = None) -> ShardedArr
 
 
 class _SumCombine:
-    """Scratch of a full sum/mean: the local partial and the combined value."""
+    """Scratch of a full sum/mean: the local partial (a 16-byte record for
+    the peer exchange), the gathered partials and the combined value."""
 
-    def __init__(self, dev: int, out_dt: _dt.Dtype) -> None:
-        self.partial = torch.empty(1, dtype=torch.float64, device=f"cuda:{dev}")
+    def __init__(self, dev: int, out_dt: _dt.Dtype, world: int = 1) -> None:
+        self.partial = torch.zeros(2, dtype=torch.float64, device=f"cuda:{dev}")
+        self.parts = torch.zeros(2 * max(1, world), dtype=torch.float64, device=f"cuda:{dev}")
         self.sum_out = empty((), out_dt, dev)
         self.mean_out = empty((), out_dt, dev)
 
@@ -103,6 +192,15 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
                          c.partial.data_ptr(), _dt.F64, cd.code, 1,
                          scratch.data_ptr() if scratch is not None else None, nbytes, stream), "sum_all")
     world, _ = _world(x.group)
+    ex = peer_exchange(dev, x.group)
+    if ex is not None:
+        # partials of all ranks over NVLink, summed in rank order on every rank
+        if c.parts.numel() < 2 * world:
+            c.parts = torch.zeros(2 * world, dtype=torch.float64, device=f"cuda:{dev}")
+        ex.allgather(c.partial, c.parts[: 2 * world], stream)
+        check(LIB.mpb_shard_sum_parts_finalize(c.parts.data_ptr(), 16, world, float(x.global_size), a.dtype.code,
+                                               c.sum_out.data_ptr, c.mean_out.data_ptr, stream), "sum_all")
+        return c.sum_out, c.mean_out
     if world > 1:
         dist.all_reduce(c.partial, op=dist.ReduceOp.SUM, group=x.group)
     check(LIB.mpb_shard_sum_finalize(c.partial.data_ptr(), float(x.global_size), a.dtype.code,
@@ -138,7 +236,13 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
     check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
                          c.rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
                          scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
-    if world > 1:
+    ex = peer_exchange(dev, x.group)
+    if ex is not None:
+        ex.allgather(c.rec, c.all, stream)
+        recs = c.all
+        row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
+        starts = [shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)]
+    elif world > 1:
         dist.all_gather_into_tensor(c.all, c.rec, group=x.group)
         recs = c.all
         row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1

@@ -23,7 +23,7 @@ def _free_port() -> int:
     return p
 
 
-def _worker(rank, world, port, x, row, out_q):
+def _worker(rank, world, port, x, row, out_q, transport="peer"):
     import datetime
 
     import torch.distributed as dist
@@ -31,6 +31,7 @@ def _worker(rank, world, port, x, row, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["MUSAPY_B200_SHARD_COLLECTIVE"] = transport
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device(f"cuda:{rank}"))
@@ -46,14 +47,23 @@ def _worker(rank, world, port, x, row, out_q):
     amax = sh.argreduce_all(xs, True)
     amin = sh.argreduce_all(xs, False)
     res = (y.local.numpy(), rs.local.numpy(), float(s.item()), float(m.item()), int(amax.item()), int(amin.item()))
-    out_q.put((rank, r0, r1, res))
+    # many exchanges in a row (sequence numbers, both buffer parities)
+    seq = []
+    for _ in range(25):
+        s2, _m2 = sh.sum_all(xs)
+        seq.append((float(s2.item()), int(sh.argreduce_all(xs, True).item())))
+    for ex in sh._EXCHANGES.values():
+        ex.check()
+    out_q.put((rank, r0, r1, res, seq))
+    sh.close_exchanges()
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
 @pytest.mark.parametrize("case", ["random", "nan_first", "nan_in_rank1", "ties"])
-def test_sharded_ops_two_gpus(oracle, case):
+def test_sharded_ops_two_gpus(oracle, case, transport):
     rng = np.random.default_rng(5)
     x = rng.random((1024, 4096), dtype=np.float32) * 2 - 1
     row = rng.random(4096, dtype=np.float32) * 2 - 1
@@ -67,7 +77,7 @@ def test_sharded_ops_two_gpus(oracle, case):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, x, row, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, x, row, q, transport)) for r in range(2)]
     for p in procs:
         p.start()
     got = [q.get(timeout=180) for _ in range(2)]
@@ -75,7 +85,10 @@ def test_sharded_ops_two_gpus(oracle, case):
         p.join(120)
         assert p.exitcode == 0
     want_y = oracle.binary("add", x, row)
-    for rank, r0, r1, (y, rs, s, m, amax, amin) in got:
+    seqs = [[repr(t) for t in g[4]] for g in got]  # repr: NaN-safe comparison
+    assert seqs[0] == seqs[1], "ranks disagree on repeated exchanges"
+    assert len(set(seqs[0])) == 1, "repeated full reductions differ"
+    for rank, r0, r1, (y, rs, s, m, amax, amin), _ in got:
         assert_bits_equal(y, want_y[r0:r1], f"sharded add rank {rank}")
         want_rs = oracle.reduce("sum", want_y[r0:r1], axis=1)
         ok = np.abs(rs.astype(np.float64) - want_rs) <= 1e-5 * np.abs(want_y[r0:r1]).astype(np.float64).sum(1)
