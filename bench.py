@@ -615,6 +615,11 @@ def run_suite(args) -> None:
         emit("NEXT", "contiguous(x[:, ::2]) f32 (8192,32768)->(8192,16384)", 2 * (q * q // 2) * 4,
              lambda: ms.contiguous(ms.slice(w, [[0, q // 2, 1], [0, 2 * q, 2]]), out=half))
         del t, f, half, w, x2
+        # one rank's local full reductions in the 8-GPU config-5 run (1 GiB)
+        s1 = ms.sum(x)
+        emit("NEXT", "sum all f32 2^28 (8-GPU shard size)", q * q * 4, lambda: ms.sum(x, out=s1), graph=True)
+        a1 = ms.argmax(x)
+        emit("NEXT", "argmax all f32 2^28 (8-GPU shard size)", q * q * 4, lambda: ms.argmax(x, out=a1), graph=True)
         n = 1 << 30
         emit("NEXT", "arange f32 2^30", n * 4, lambda: ms.arange(0, n, 1, dtype="f32"))
         emit("NEXT", "linspace f64 2^28", (1 << 28) * 8, lambda: ms.linspace(-1.0, 1.0, 1 << 28))

@@ -111,6 +111,8 @@ struct PArg {
       a = Acc{v, idx};
   }
   MPB_D static Acc merge(const Acc& l, const Acc& r) { return better(r.v, r.i, l) ? r : l; }
+  // strictly better value (ties keep the earlier one)
+  MPB_D static bool beats(V m, V b) { return IS_MAX ? (m > b) : (m < b); }
   // NaN-ignoring extreme of two values (fmax/fmin return the non-NaN one).
   MPB_D static V pick(V a, V b) {
     if constexpr (std::is_same<V, int64_t>::value) {
@@ -357,13 +359,19 @@ MPB_D typename P::Acc ext_zero_fix_thread(typename P::Acc acc, const typename P:
 }
 
 // ------------------------------------------------- ROW: warp per output
+template <class A> struct AccValue { using type = A; };
+template <class V> struct AccValue<ArgAcc<V>> { using type = V; };
+
 template <class P, int VEC>
 MPB_D void fold_segment_vec(typename P::Acc& acc, const typename P::In* __restrict__ p, int64_t li, int64_t lbase,
                             int64_t rwi, int lane, int nthreads, int tid) {
   using In = typename P::In;
+  using V = typename AccValue<typename P::Acc>::type;
   constexpr int UNR = 4;
   const int64_t step = (int64_t)nthreads * VEC;
   int64_t c = (int64_t)tid * VEC;
+  V best{};
+  int64_t cbest = -1;  // start of the group that first reached `best` (arg policies)
   for (; c + (UNR - 1) * step < li; c += UNR * step) {
     uint4 w[UNR][(VEC * sizeof(In) + 15) / 16];
 #pragma unroll
@@ -373,24 +381,22 @@ MPB_D void fold_segment_vec(typename P::Acc& acc, const typename P::In* __restri
         w[u][k] = ld_stream16(reinterpret_cast<const char*>(p + c + u * step) + 16 * k);
     }
     if constexpr (P::kArg) {
-      // Extreme of the UNR*VEC values first (one min/max per element); the
-      // exact in-order (value, index) rule runs only when it can matter.
-      auto m = P::pick(cvt<decltype(acc.v)>(reinterpret_cast<const In*>(w[0])[0]),
-                       cvt<decltype(acc.v)>(reinterpret_cast<const In*>(w[0])[VEC > 1 ? 1 : 0]));
+      // Extreme of the UNR*VEC values (one min/max per element); only which
+      // group first reached the best value is remembered (selects, no
+      // branch), and that group is re-read once at the end of the segment.
+      V m = P::pick(cvt<V>(reinterpret_cast<const In*>(w[0])[0]),
+                    cvt<V>(reinterpret_cast<const In*>(w[0])[VEC > 1 ? 1 : 0]));
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
         const In* v = reinterpret_cast<const In*>(w[u]);
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) m = P::pick(m, cvt<decltype(acc.v)>(v[j]));
+        for (int j = 0; j < VEC; ++j) m = P::pick(m, cvt<V>(v[j]));
       }
-      if (P::improves(m, acc, lbase + c * rwi)) {
-#pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-          const In* v = reinterpret_cast<const In*>(w[u]);
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) P::fold(acc, v[j], lbase + (c + u * step + j) * rwi);
-        }
-      }
+      // the first non-NaN group, then strictly better ones (an all-NaN group
+      // gives m = NaN, which never wins)
+      const bool take = cbest < 0 ? !is_nan_v<V>(m) : P::beats(m, best);
+      best = take ? m : best;
+      cbest = take ? c : cbest;
     } else {
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
@@ -398,6 +404,29 @@ MPB_D void fold_segment_vec(typename P::Acc& acc, const typename P::In* __restri
 #pragma unroll
         for (int j = 0; j < VEC; ++j) P::fold(acc, v[j], lbase + (c + u * step + j) * rwi);
       }
+    }
+  }
+  if constexpr (P::kArg) {
+    if (cbest >= 0) {
+      // first element of the best group equal to the best value (it exists:
+      // the group's extreme is one of its elements), merged with the rule
+      int64_t idx = 0;
+      bool found = false;
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        uint4 w[(VEC * sizeof(In) + 15) / 16];
+#pragma unroll
+        for (int k = 0; k < (int)((VEC * sizeof(In) + 15) / 16); ++k)
+          w[k] = ld_nc16(reinterpret_cast<const char*>(p + cbest + u * step) + 16 * k);
+        const In* v = reinterpret_cast<const In*>(w);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const bool hit = !found && cvt<V>(v[j]) == best;
+          idx = hit ? lbase + (cbest + u * step + j) * rwi : idx;
+          found = found || hit;
+        }
+      }
+      acc = P::merge(acc, typename P::Acc{best, idx});
     }
   }
   for (; c < li; c += step) {
