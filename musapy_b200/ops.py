@@ -56,9 +56,15 @@ def _scalar_like(x, other: Array) -> Array:
             d = _dt.complex128
         elif isinstance(x, float) and not (d.is_floating() or d.is_complex()):
             d = _dt.float64
+        v = complex(x)
+        if isinstance(x, (bool, np.bool_)) or (isinstance(x, numbers.Integral) and builtins.abs(int(x)) <= (1 << 53)) \
+                or not isinstance(x, numbers.Integral):
+            # written on the device by the fill kernel: no host -> device copy
+            # (which would wait for the host) in the middle of a stream of ops
+            return full((), v if d.is_complex() else v.real, d, other._dev)
         from .array import array as _array
 
-        return _array(x, dtype=d, device=other._dev)
+        return _array(x, dtype=d, device=other._dev)  # integers beyond 2^53: exact host conversion
     raise TypeError(f"unsupported operand {type(x).__name__}")
 
 

@@ -505,3 +505,24 @@ def test_f16_pow_special_values(ms, oracle):
     a, b = np.meshgrid(v, v)
     got = ms.pow(dev(ms, a), dev(ms, b)).numpy()
     assert_ulp(got, oracle.binary("pow", a, b), 2, "f16 pow specials")
+
+
+@pytest.mark.parametrize("dtype,scalar", [(np.float32, 2.5), (np.float64, -1.0 / 3.0), (np.float16, 0.1),
+                                          (np.int64, 2.5), (np.int32, -0.5), (np.float64, (1 << 60) + 3),
+                                          (np.complex64, 1 + 2j), (np.float32, 3), (np.float32, 1e-46)])
+def test_python_scalar_operands(ms, oracle, dtype, scalar):
+    """Python scalars take the array operand's dtype (complex / float scalars
+    widen integer arrays), are written on the device, and give the same bits as
+    the oracle with the scalar as a 0-d array of that dtype."""
+    rng = np.random.default_rng(50)
+    x = rng.standard_normal(1000) * 10
+    x = (x + 1j * rng.standard_normal(1000)).astype(dtype) if np.dtype(dtype).kind == "c" else \
+        (x.astype(dtype) if np.dtype(dtype).kind == "f" else np.abs(x).astype(dtype))
+    xd = dev(ms, x)
+    got = ms.mul(xd, scalar)
+    d = got.dtype
+    want = oracle.binary("mul", x, np.array(scalar, dtype=ms.dtypes.to_numpy(d)), all_gpu=True)
+    assert_bits_equal(got.numpy(), want, f"{dtype} * {scalar!r}")
+    got_r = ms.sub(scalar, xd).numpy()
+    want_r = oracle.binary("sub", np.array(scalar, dtype=ms.dtypes.to_numpy(d)), x, all_gpu=True)
+    assert_bits_equal(got_r, want_r, f"{scalar!r} - {dtype}")
