@@ -236,6 +236,7 @@ def run_b200(args) -> None:
     import musapy_b200 as ms
     from musapy_b200 import shard as sh
 
+    ms.set_default_device(f"cuda:{local}")
     rows, cols = args.rows, COLS
     r0, r1 = shard_rows(rows, world, rank)
     nloc = r1 - r0
@@ -356,7 +357,8 @@ def run_b200(args) -> None:
 
     if world > 1:
         for ex in list(sh._EXCHANGES.values()):
-            ex.check()  # a peer-exchange wait that gave up invalidates the run
+            if ex is not None:
+                ex.check()  # a peer-exchange wait that gave up invalidates the run
         sh.close_exchanges()
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -428,6 +430,7 @@ def run_suite(args) -> None:
 
     import musapy_b200 as ms
 
+    ms.set_default_device("cuda:0")
     peak, peak_kind = measured_peak()
     stream = torch.cuda.current_stream()
 

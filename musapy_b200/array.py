@@ -17,8 +17,6 @@ from . import dtypes as _dt
 from . import errors
 from . import streams as _streams
 
-_DEFAULT_DEVICE = [0]
-_DEFAULT_DTYPE = [_dt.float32]
 # host transfers from this size on go through the pinned staging ring
 # (mpb_copy_h2d / mpb_copy_d2h); smaller ones through torch's copy
 _STAGED_COPY_BYTES = 1 << 20
@@ -26,15 +24,24 @@ _STAGED_COPY_BYTES = 1 << 20
 
 class Device:
     """A CUDA device. "musa:N" is accepted as an alias of "cuda:N" so that
-    musapy call sites keep working."""
+    musapy call sites keep working. A device taken from an array carries how
+    it was resolved (`resolution_source`: arg / context / input_array /
+    global_default, rust/musapy-python/src/device.rs:40-90)."""
 
-    __slots__ = ("index",)
+    __slots__ = ("index", "_source")
 
-    def __init__(self, spec="cuda:0") -> None:
+    def __init__(self, spec="cuda:0", _source=None) -> None:
         self.index = parse_device(spec)
+        self._source = _source
 
     def __repr__(self) -> str:
-        return f"Device('cuda:{self.index}')"
+        if self._source:
+            return f"Device(cuda:{self.index})  # resolved from: {self._source}"
+        return f"Device(cuda:{self.index})"
+
+    @property
+    def resolution_source(self):
+        return self._source
 
     def __str__(self) -> str:
         return f"cuda:{self.index}"
@@ -59,9 +66,12 @@ class Device:
     def is_cuda(self) -> bool:
         return True
 
+    @property
     def is_musa(self) -> bool:
+        """True: the accelerator device (device.rs:64-68)."""
         return True
 
+    @property
     def musa_id(self) -> int:
         return self.index
 
@@ -94,11 +104,13 @@ def parse_device(spec) -> int:
 
 
 def set_default_device(spec) -> None:
-    _DEFAULT_DEVICE[0] = parse_device(spec)
+    """``ms.set_default_device`` (resolution.rs:60-75): this thread's default
+    device, inherited by threads that have not chosen one."""
+    _streams.set_default_device(parse_device(spec))
 
 
 def set_default_dtype(spec) -> None:
-    _DEFAULT_DTYPE[0] = _dt.parse(spec)
+    _streams.set_default_dtype(_dt.parse(spec))
 
 
 def default_dtype() -> _dt.Dtype:
@@ -125,9 +137,10 @@ def _prod(xs: Iterable[int]) -> int:
 class Array:
     """A strided view of device memory."""
 
-    __slots__ = ("_buf", "_shape", "_strides", "_offset", "_dtype", "_dev", "_name")
+    __slots__ = ("_buf", "_shape", "_strides", "_offset", "_dtype", "_dev", "_name", "_dev_src", "_dt_src")
 
-    def __init__(self, buf: torch.Tensor, shape, strides, offset: int, dtype: _dt.Dtype, device: int) -> None:
+    def __init__(self, buf: torch.Tensor, shape, strides, offset: int, dtype: _dt.Dtype, device: int,
+                 dev_src: str = "input_array", dt_src: str = "input_array") -> None:
         self._buf = buf  # torch uint8 tensor owning the allocation
         self._shape = tuple(int(s) for s in shape)
         self._strides = tuple(int(s) for s in strides)
@@ -135,6 +148,8 @@ class Array:
         self._dtype = dtype
         self._dev = int(device)
         self._name = None
+        self._dev_src = dev_src  # how the device / dtype were resolved
+        self._dt_src = dt_src
 
     # ------------------------------------------------------------ metadata
     @property
@@ -164,7 +179,12 @@ class Array:
 
     @property
     def device(self) -> Device:
-        return Device(self._dev)
+        return Device(self._dev, self._dev_src)
+
+    @property
+    def dtype_resolution_source(self) -> str:
+        """arg / context / input_array / global_default / auto_probe (array.rs:59-63)."""
+        return self._dt_src
 
     @property
     def nbytes(self) -> int:
@@ -379,13 +399,13 @@ def empty(shape, dtype=None, device=None) -> Array:
     shape = tuple(int(s) for s in shape)
     if any(s < 0 for s in shape):
         raise errors.ShapeError(f"negative dimension in {shape}")
-    d = _dt.parse(dtype) if dtype is not None else default_dtype()
-    dev = parse_device(device)
+    d, dt_src = _streams.resolve_dtype(dtype)
+    dev, dev_src = _streams.resolve_device(device)
     n = _prod(shape) * d.itemsize
     # Round allocations up to 16 bytes so every buffer start is vector aligned.
     buf = torch.empty(max(16, (n + 15) // 16 * 16), dtype=torch.uint8, device=f"cuda:{dev}")
     buf._mpb_owner = _streams.current_stream(dev).torch_stream  # the stream the array belongs to
-    return Array(buf, shape, contiguous_strides(shape), 0, d, dev)
+    return Array(buf, shape, contiguous_strides(shape), 0, d, dev, dev_src, dt_src)
 
 
 def _has_complex(data) -> bool:
@@ -454,10 +474,11 @@ def array(data, dtype=None, device=None) -> Array:
         return from_numpy(data.detach().cpu().numpy(), device, dtype)
     if isinstance(data, np.ndarray):
         return from_numpy(data, device, dtype)
-    if dtype is None:
-        d = _dt.complex128 if _has_complex(data) else default_dtype()
+    if dtype is None and _has_complex(data):
+        d, dt_src = _dt.complex128, "input_array"
     else:
-        d = _dt.parse(dtype)
+        d, dt_src = _streams.resolve_dtype(dtype)
+    dev, dev_src = _streams.resolve_device(device)
     if d.code == _dt.BF16:
         host = _np_cast(np.asarray(data, dtype=np.float64), d)
     elif d.is_complex():
@@ -467,7 +488,9 @@ def array(data, dtype=None, device=None) -> Array:
         if host.dtype.kind == "c":
             raise errors.DtypeError(f"complex data cannot be stored as {d}")
         host = host.astype(_dt.to_numpy(d))
-    return from_numpy(host, device, d)
+    out = from_numpy(host, dev, d)
+    out._dev_src, out._dt_src = dev_src, dt_src
+    return out
 
 
 def from_torch(t: torch.Tensor) -> Array:
@@ -486,7 +509,7 @@ def from_dlpack(obj) -> Array:
 
 # -------------------------------------------------------------------- views
 def _view(a: Array, shape, strides, offset) -> Array:
-    return Array(a._buf, shape, strides, offset, a._dtype, a._dev)
+    return Array(a._buf, shape, strides, offset, a._dtype, a._dev, a._dev_src, a._dt_src)
 
 
 def transpose(a: Array, axes=None) -> Array:

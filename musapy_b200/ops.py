@@ -38,6 +38,14 @@ def _stream(dev: int) -> int:
     return _streams.current_stream(dev).cuda_stream
 
 
+def _out(shape, d, dev: int) -> Array:
+    """An op's result: device and dtype follow the inputs (input_array in
+    musapy's resolution chain, resolution.rs:224-230)."""
+    res = empty(shape, d, dev)
+    res._dev_src = res._dt_src = "input_array"
+    return res
+
+
 def _launch(op: str, dev: int, *arrays) -> int:
     """CUDA stream for a launch of `op` touching `arrays` on `dev`: waits for
     other streams' pending work on those buffers, checks the stream is not
@@ -157,7 +165,7 @@ def _binary(name: str, a, b, out):
             raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
         res = out
     else:
-        res = empty(shape, d, dev)
+        res = _out(shape, d, dev)
     n = len(shape)
     rc = LIB.mpb_elementwise(
         OPS[name], n, i64arr(shape),
@@ -204,7 +212,7 @@ def _compare(name: str, a, b, out):
             raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
         res = out
     else:
-        res = empty(shape, _dt.bool_, dev)
+        res = _out(shape, _dt.bool_, dev)
     rc = LIB.mpb_elementwise(
         OPS[name], len(shape), i64arr(shape),
         a.data_ptr, a.dtype.code, i64arr(_bstrides(a, shape)),
@@ -258,7 +266,7 @@ def _unary(name: str, a: Array, out, p0: float = 0.0, p1: float = 0.0):
             raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
         res = out
     else:
-        res = empty(a.shape, out_d, dev)
+        res = _out(a.shape, out_d, dev)
     rc = LIB.mpb_elementwise(
         OPS[name], a.ndim, i64arr(a.shape), a.data_ptr, d.code, i64arr(a.strides),
         None, 0, None, res.data_ptr, out_d.code, d.code, float(p0), float(p1), _launch(name, dev, a, res),
@@ -315,7 +323,7 @@ def _validate_cast(src: _dt.Dtype, dst: _dt.Dtype) -> None:
 
 def _cast_into(a: Array, d: _dt.Dtype, out: Array | None = None) -> Array:
     dev = a._dev
-    res = out if out is not None else empty(a.shape, d, dev)
+    res = out if out is not None else _out(a.shape, d, dev)
     rc = LIB.mpb_elementwise(
         OPS["cast"], a.ndim, i64arr(a.shape), a.data_ptr, a.dtype.code, i64arr(a.strides),
         None, 0, None, res.data_ptr, d.code, d.code, 0.0, 0.0, _launch("cast", dev, a, res),
@@ -438,7 +446,7 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
             raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
         res = out
     else:
-        res = empty(out_shape, out_d, dev)
+        res = _out(out_shape, out_d, dev)
     if M == 0:
         return res
     if L == 0:
@@ -532,7 +540,7 @@ def cumsum(a, axis=None, out=None):
             raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
         res = out
     else:
-        res = empty(shape, cd, dev)
+        res = _out(shape, cd, dev)
     if src.size == 0:
         return res
     shape_c, strides_c = i64arr(shape), i64arr(src.strides)

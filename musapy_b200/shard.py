@@ -66,31 +66,50 @@ class PeerExchange:
     same order everywhere (as collectives already must be)."""
 
     def __init__(self, dev: int, group=None) -> None:
+        """Collective: every rank of `group` constructs it together. Raises
+        InteropError on every rank when any rank cannot share or map the
+        buffers (the ranks agree before and after mapping)."""
         import ctypes
 
         self.dev, self.group = dev, group
         self.world, self.rank = _world(group)
         self.seq = 0
         self._buf = ctypes.c_void_p()
+        self._opened = []
         handle = ctypes.create_string_buffer(int(LIB.mpb_peer_handle_bytes()))
         with torch.cuda.device(dev):
-            check(LIB.mpb_peer_alloc(ctypes.byref(self._buf), handle), "peer exchange")
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle.raw, group=group)
+            ok = LIB.mpb_peer_alloc(ctypes.byref(self._buf), handle) == 0
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, (ok, handle.raw if ok else b""), group=group)
+        if not all(g[0] for g in gathered):
+            self._release()
+            raise errors.InteropError("peer exchange: a rank could not allocate or share its buffer")
         ptrs = []
-        self._opened = []
         with torch.cuda.device(dev):
-            for r, h in enumerate(handles):
+            for r, (_, h) in enumerate(gathered):
                 if r == self.rank:
                     ptrs.append(self._buf.value)
                     continue
                 p = ctypes.c_void_p()
                 hb = ctypes.create_string_buffer(h, len(h))
-                check(LIB.mpb_peer_open(hb, ctypes.byref(p)), "peer exchange")
+                if LIB.mpb_peer_open(hb, ctypes.byref(p)) != 0:
+                    ok = False
+                    break
                 self._opened.append(p.value)
                 ptrs.append(p.value)
+        oks = [None] * self.world
+        dist.all_gather_object(oks, ok, group=group)
+        if not all(oks):
+            self._release()
+            raise errors.InteropError("peer exchange: a rank could not map the other ranks' buffers")
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+
+    def _release(self) -> None:
+        with torch.cuda.device(self.dev):
+            for p in self._opened:
+                LIB.mpb_peer_close(p)
+            self._opened = []
 
     def allgather(self, rec: torch.Tensor, out: torch.Tensor, stream: int) -> None:
         """rec: 16 or 32 bytes on this rank's device; out: world x that, in rank order."""
@@ -108,11 +127,12 @@ class PeerExchange:
         exchange kernel is still writing into anyone's buffer), then unmaps."""
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
-        with torch.cuda.device(self.dev):
-            for p in self._opened:
-                LIB.mpb_peer_close(p)
-            self._opened = []
+        self._release()
         dist.barrier(group=self.group)
+        if self._buf.value:  # nobody maps it any more
+            with torch.cuda.device(self.dev):
+                LIB.mpb_peer_free(self._buf)
+            self._buf.value = None
 
 
 _EXCHANGES: dict = {}
@@ -130,9 +150,16 @@ def peer_exchange(dev: int, group=None) -> PeerExchange | None:
     if dist.get_backend(group) != "nccl":  # CPU process groups (gloo) have no device buffers
         return None
     key = (dev, id(group))
-    ex = _EXCHANGES.get(key)
-    if ex is None:
-        ex = _EXCHANGES[key] = PeerExchange(dev, group)
+    if key in _EXCHANGES:
+        return _EXCHANGES[key]
+    try:
+        ex = PeerExchange(dev, group)
+    except errors.InteropError as e:  # every rank takes this branch together
+        import warnings
+
+        warnings.warn(f"{e}; full reductions use NCCL collectives", RuntimeWarning)
+        ex = None
+    _EXCHANGES[key] = ex
     return ex
 
 
@@ -140,7 +167,9 @@ def close_exchanges() -> None:
     """Collective teardown of every peer exchange (call on all ranks before
     destroy_process_group)."""
     for key in list(_EXCHANGES):
-        _EXCHANGES.pop(key).close()
+        ex = _EXCHANGES.pop(key)
+        if ex is not None:
+            ex.close()
 
 
 def _world(group) -> tuple[int, int]:

@@ -281,19 +281,77 @@ def dtype(spec) -> _DtypeContext:
     return _DtypeContext(spec)
 
 
-def default_device() -> int:
+# ---------------------------------------------------------- resolution
+# resolution.rs:1-120 (ADR L0-6..L0-11): the default device and dtype are
+# per thread; set_default_* writes the calling thread's value and, until the
+# thread has taken its snapshot, the process-wide seed; a thread without a
+# value snapshots the seed on first use and is independent afterwards. The
+# device has no fallback (DeviceNotConfiguredError), the dtype falls back to
+# float32.
+_seed = {"device": None, "dtype": None}
+_seed_lock = threading.Lock()
+
+
+def _get_default(kind: str):
+    v = getattr(_tls, kind + "_default", None)
+    if v is not None:
+        return v
+    with _seed_lock:
+        v = _seed[kind]
+    if v is not None:
+        setattr(_tls, kind + "_default", v)
+        setattr(_tls, kind + "_snap", True)
+    return v
+
+
+def _set_default(kind: str, value) -> None:
+    setattr(_tls, kind + "_default", value)
+    if not getattr(_tls, kind + "_snap", False):
+        with _seed_lock:
+            _seed[kind] = value
+
+
+def set_default_device(dev: int) -> None:
+    _set_default("device", dev)
+
+
+def set_default_dtype(dt: _dt.Dtype) -> None:
+    _set_default("dtype", dt)
+
+
+def resolve_device(arg=None) -> tuple[int, str]:
+    """(device index, source): arg > context > global_default >
+    DeviceNotConfiguredError (resolution.rs:200-235)."""
+    from .array import parse_device
+
+    if arg is not None:
+        return parse_device(arg), "arg"
     st = _stack("devices")
     if st:
-        return st[-1]
-    from .array import _DEFAULT_DEVICE
+        return st[-1], "context"
+    d = _get_default("device")
+    if d is not None:
+        return d, "global_default"
+    raise errors.DeviceNotConfiguredError(
+        "no device: pass device=..., use `with ms.device(...)`, or call ms.set_default_device('musa:0')")
 
-    return _DEFAULT_DEVICE[0]
+
+def resolve_dtype(arg=None) -> tuple[_dt.Dtype, str]:
+    """(dtype, source): arg > context > global_default > float32 (resolution.rs:240-262)."""
+    if arg is not None:
+        return _dt.parse(arg), "arg"
+    st = _stack("dtypes")
+    if st:
+        return st[-1], "context"
+    d = _get_default("dtype")
+    if d is not None:
+        return d, "global_default"
+    return _dt.float32, "auto_probe"  # the float32 fallback
+
+
+def default_device() -> int:
+    return resolve_device()[0]
 
 
 def default_dtype() -> _dt.Dtype:
-    st = _stack("dtypes")
-    if st:
-        return st[-1]
-    from .array import _DEFAULT_DTYPE
-
-    return _DEFAULT_DTYPE[0]
+    return resolve_dtype()[0]

@@ -39,6 +39,11 @@ def oracle():
 
 @pytest.fixture(scope="session")
 def ms():
+    import torch
+
     import musapy_b200 as ms
 
+    if torch.cuda.is_available():
+        # musapy has no implicit device (DeviceNotConfiguredError until one is set)
+        ms.set_default_device("cuda:0")
     return ms

@@ -38,6 +38,8 @@ def _worker(rank, world, port, x, row, out_q, transport="peer"):
     import musapy_b200 as ms
     from musapy_b200 import shard as sh
 
+    ms.set_default_device(f"cuda:{rank}")
+
     r0, r1 = sh.shard_rows(x.shape[0], world, rank)
     xs = sh.ShardedArray(ms.from_numpy(x[r0:r1], device=rank), x.shape, r0)
     rd = ms.from_numpy(row, device=rank)
@@ -53,7 +55,8 @@ def _worker(rank, world, port, x, row, out_q, transport="peer"):
         s2, _m2 = sh.sum_all(xs)
         seq.append((float(s2.item()), int(sh.argreduce_all(xs, True).item())))
     for ex in sh._EXCHANGES.values():
-        ex.check()
+        if ex is not None:
+            ex.check()
     out_q.put((rank, r0, r1, res, seq))
     sh.close_exchanges()
     dist.barrier(device_ids=[rank])

@@ -138,6 +138,7 @@ def test_stream_context_requires_stream():
 def test_device_and_dtype_contexts_nest_and_restore():
     from musapy_b200.array import default_dtype, parse_device
 
+    ms.set_default_device("musa:0")
     base_dev, base_dt = parse_device(None), default_dtype()
     with ms.device("musa:2") as d:
         assert d == "cuda:2" and parse_device(None) == 2
@@ -177,3 +178,56 @@ def test_contexts_are_per_thread():
 def test_device_context_rejects_cpu():
     with pytest.raises(ms.DeviceError):
         ms.device("cpu")
+
+
+def test_resolution_chain_sources():
+    """resolve_device / resolve_dtype: arg > context > global_default
+    (resolution.rs:200-262); dtype falls back to float32 (auto_probe)."""
+    import subprocess
+    import sys
+
+    code = ("import musapy_b200 as ms\n"
+            "try:\n"
+            "    ms.streams.resolve_device()\n"
+            "    print('NO_ERROR')\n"
+            "except ms.DeviceNotConfiguredError as e:\n"
+            "    print('DeviceNotConfiguredError')\n"
+            "print(ms.streams.resolve_dtype())\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300).stdout
+    assert "DeviceNotConfiguredError" in out and "NO_ERROR" not in out
+    assert "auto_probe" in out and "float32" in out
+    assert issubclass(ms.DeviceNotConfiguredError, ms.DeviceError)
+    ms.set_default_device("cuda:1")
+    assert streams.resolve_device() == (1, "global_default")
+    assert streams.resolve_device("musa:3") == (3, "arg")
+    with ms.device("cuda:2"):
+        assert streams.resolve_device() == (2, "context")
+        assert streams.resolve_device(0) == (0, "arg")
+    with ms.dtype("f64"):
+        assert streams.resolve_dtype() == (ms.float64, "context")
+        assert streams.resolve_dtype("f16") == (ms.float16, "arg")
+    ms.set_default_device("cuda:0")
+
+
+def test_default_device_thread_inheritance():
+    """A new thread snapshots the process seed on first use; its own
+    set_default_device does not reach the parent (resolution.rs:55-100)."""
+    ms.set_default_device("cuda:0")
+    seen = {}
+
+    def child():
+        seen["inherited"] = streams.resolve_device()
+        ms.set_default_device("cuda:3")
+        seen["own"] = streams.resolve_device()
+
+    th = threading.Thread(target=child)
+    th.start()
+    th.join(10)
+    assert seen["inherited"] == (0, "global_default") and seen["own"] == (3, "global_default")
+    assert streams.resolve_device() == (0, "global_default")
+
+
+def test_device_properties_match_binding():
+    d = ms.Device("musa:1")
+    assert d.is_musa is True and d.musa_id == 1 and str(d) == "cuda:1"
+    assert repr(d) == "Device(cuda:1)" and d.resolution_source is None

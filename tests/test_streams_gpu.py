@@ -146,3 +146,42 @@ def test_from_numpy_views_and_complex(ms):
     assert np.array_equal(d.numpy(), v)
     z = ms.from_numpy(np.float32(2.5))
     assert z.shape == () and z.item() == 2.5
+
+
+def test_resolution_sources_on_arrays(ms):
+    """The reference's resolution tests (tests/python/test_resolution.py:23-160)
+    on the CUDA device: repr(a.device) names how the device was chosen, the
+    dtype context sets the default dtype, op results follow their inputs."""
+    import threading
+
+    ms.set_default_device("cuda:0")
+    a = ms.array([1.0, 2.0], dtype="f32", device="cuda:0")
+    assert "resolved from: arg" in repr(a.device)
+    b = ms.array([1.0, 2.0], dtype="f32")
+    assert "resolved from: global_default" in repr(b.device)
+    with ms.device("cuda:0"):
+        c = ms.array([1.0], dtype="f32")
+        assert "resolved from: context" in repr(c.device)
+        with ms.device("musa:0"):
+            assert "context" in repr(ms.array([1.0], dtype="f32").device)
+    assert "global_default" in repr(ms.array([1.0], dtype="f32").device)
+    with ms.dtype("f64"):
+        d = ms.array([1.0, 2.0])
+        assert d.dtype == "f64" and d.dtype_resolution_source == "context"
+    e = ms.array([1.0, 2.0])
+    assert e.dtype == "f32" and e.dtype_resolution_source == "auto_probe"
+    s = ms.Stream("cuda:0", priority=0)
+    with ms.stream(s):
+        f = ms.array([1.0], dtype="f32")
+        assert f.stream.priority == 0 and f.stream == s
+    g = ms.add(a, b)
+    assert g.device.resolution_source == "input_array" and g.dtype_resolution_source == "input_array"
+    out = {}
+
+    def worker():
+        out["dev"] = str(ms.array([1.0], dtype="f32").device)
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join(30)
+    assert out["dev"] == "cuda:0"
