@@ -139,3 +139,39 @@ def test_config4_complex64_mul(ms, oracle, c4):
     z = ms.mul(ms.from_numpy(z1), ms.from_numpy(z2))
     idx = np.random.default_rng(26).choice(z1.size, 1 << 20, replace=False)
     assert_bits_equal(z.numpy()[idx], oracle.binary("mul", z1[idx], z2[idx]), "c64 mul")
+
+
+def test_config5_full_size_reductions(ms):
+    """Config 5 on one GPU (2^31 f32, 8 GiB): argmax/argmin with the winner
+    planted near the last index, 2^31 - 12345 (no 32-bit wrap anywhere in the
+    split kernels' index arithmetic), and the
+    full sum/mean against an f64 truth computed on the device by torch."""
+    import torch
+
+    import bench
+
+    rows, cols = bench.ROWS, bench.COLS
+    x = ms.empty((rows, cols), "f32")
+    host = np.empty((4096, cols), np.float32)
+    for r0 in range(0, rows, 4096):
+        bench.gen_rows(r0, r0 + 4096, cols, out=host)
+        x.torch()[r0:r0 + 4096].copy_(torch.from_numpy(host))
+    t = x.torch()
+    big = (1 << 31) - 12345
+    r, c = divmod(big, cols)
+    t[r, c] = 5.0
+    t[r, c + 100] = 5.0      # a later tie: the first occurrence must win
+    t[r - 7, 11] = -5.0
+    assert ms.argmax(x).item() == big
+    assert ms.argmin(x).item() == (r - 7) * cols + 11
+    s, m = ms.sum(x).item(), ms.mean(x).item()
+    rs = ms.sum(x, axis=1).torch().double()
+    td = t.double()
+    want = td.sum(dim=1)
+    td.abs_()
+    bound = 1e-5 * td.sum(dim=1)
+    truth, absum = want.sum().item(), bound.sum().item() / 1e-5
+    del td
+    assert abs(s - truth) <= 1e-5 * absum
+    assert abs(m - truth / t.numel()) <= 1e-5 * absum / t.numel()
+    assert bool(((rs - want).abs() <= bound).all())
