@@ -603,7 +603,7 @@ def run_suite(args) -> None:
              cpu=(lambda: O.binary("mul", z1s, z2s), m * 24, "first 2^22 elements"))
         del z1, z2, z, d
     if "NEXT" in cfgs:
-        # the survey's "next" rows: contiguous copies of views, creation
+        # the rows around the hot path: contiguous copies of views, creation
         # kernels, host <-> device transfers (device-side bytes = read + write)
         q = 16384
         x = ms.arange(q * q, dtype="f32")
