@@ -132,6 +132,27 @@ def _load() -> ctypes.CDLL:
 LIB = _load()
 
 
+def _load_native():
+    """The compiled per-op binding (csrc/native_module.cpp). It links
+    against the library file loaded above, which the dynamic loader maps
+    once: both routes share one library state."""
+    import importlib.machinery
+    import importlib.util
+    import sysconfig
+
+    path = os.path.join(_HERE, "_lib", "_native" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with `python musapy_b200/build.py`")
+    loader = importlib.machinery.ExtensionFileLoader("musapy_b200._native", path)
+    spec = importlib.util.spec_from_file_location("musapy_b200._native", path, loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+NATIVE = _load_native()
+
+
 _I64_TYPES = [ctypes.c_int64 * max(1, n) for n in range(33)]
 
 

@@ -230,8 +230,8 @@ class Array:
         """The stream the array was created on (array.rs:73); for arrays that
         wrap foreign memory, the stream that last used it, else the current
         stream of its device."""
-        ts = getattr(self._buf, "_mpb_owner", None) or getattr(self._buf, "_mpb_stream", None)
-        return _streams._wrap(self._dev, ts) if ts is not None else _streams.current_stream(self._dev)
+        s = getattr(self._buf, "_mpb_owner", None) or getattr(self._buf, "_mpb_stream", None)
+        return s if s is not None else _streams.current_stream(self._dev)
 
     def __len__(self) -> int:
         if not self._shape:
@@ -401,11 +401,41 @@ def empty(shape, dtype=None, device=None) -> Array:
         raise errors.ShapeError(f"negative dimension in {shape}")
     d, dt_src = _streams.resolve_dtype(dtype)
     dev, dev_src = _streams.resolve_device(device)
-    n = _prod(shape) * d.itemsize
+    return _alloc(shape, d, dev, dev_src, dt_src)
+
+
+_LAYOUTS: dict = {}
+_TORCH_DEVICES: dict = {}
+_new_object = object.__new__
+
+
+def _alloc(shape: tuple, d: _dt.Dtype, dev: int, dev_src: str, dt_src: str) -> Array:
+    """A fresh C-contiguous array. `shape` is a tuple of non-negative Python
+    ints and `dev` a resolved device index (the per-op output path: no
+    parsing, cached strides)."""
+    lay = _LAYOUTS.get(shape)
+    if lay is None:
+        if len(_LAYOUTS) >= 4096:
+            _LAYOUTS.clear()
+        lay = _LAYOUTS[shape] = (contiguous_strides(shape), _prod(shape))
+    tdev = _TORCH_DEVICES.get(dev)
+    if tdev is None:
+        tdev = _TORCH_DEVICES[dev] = torch.device("cuda", dev)
+    n = lay[1] * d.itemsize
     # Round allocations up to 16 bytes so every buffer start is vector aligned.
-    buf = torch.empty(max(16, (n + 15) // 16 * 16), dtype=torch.uint8, device=f"cuda:{dev}")
-    buf._mpb_owner = _streams.current_stream(dev).torch_stream  # the stream the array belongs to
-    return Array(buf, shape, contiguous_strides(shape), 0, d, dev, dev_src, dt_src)
+    buf = torch.empty(max(16, (n + 15) & ~15), dtype=torch.uint8, device=tdev)
+    buf._mpb_owner = _streams.current_stream(dev)  # the stream the array belongs to
+    a = _new_object(Array)
+    a._buf = buf
+    a._shape = shape
+    a._strides = lay[0]
+    a._offset = 0
+    a._dtype = d
+    a._dev = dev
+    a._name = None
+    a._dev_src = dev_src
+    a._dt_src = dt_src
+    return a
 
 
 def _has_complex(data) -> bool:

@@ -1,7 +1,9 @@
 """Build libmusapy_b200.so in-tree for sm_100a.
 
 Every ``.cu`` under ``csrc/`` is compiled to an object by ``nvcc`` (in
-parallel) and linked into ``musapy_b200/_lib/libmusapy_b200.so``. Objects are
+parallel) and linked into ``musapy_b200/_lib/libmusapy_b200.so``; then
+``csrc/native_module.cpp``, the CPython binding of the per-op calls, is
+compiled by ``g++`` against it into ``musapy_b200/_lib/_native*.so``. Objects are
 rebuilt only when a source or header is newer than the object, so repeated
 calls are cheap. The CUDA runtime is linked dynamically, so the library
 shares one runtime (and one error state) with the host process.
@@ -20,6 +22,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -107,11 +110,37 @@ def build(force: bool = False, jobs: int | None = None, extra: list[str] | None 
         cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "shared", "-o", lib] + objs + [
             "-Xlinker",
             f"-rpath={CUDA_HOME}/lib64",
+            "-Xlinker",
+            f"-soname={LIBNAME}",
         ]
         p = subprocess.run(cmd, capture_output=True, text=True)
         if p.returncode != 0:
             raise RuntimeError("link failed:\n" + p.stdout + p.stderr)
+    build_native(force=force)
     return lib
+
+
+def native_path() -> str:
+    return os.path.join(LIBDIR, "_native" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_native(force: bool = False) -> str:
+    """The CPython binding of the per-op entry points (csrc/native_module.cpp),
+    linked against the library beside it."""
+    src = os.path.join(CSRC, "native_module.cpp")
+    out = native_path()
+    deps = [src, lib_path(), os.path.join(INCLUDE, "musapy_b200.h")]
+    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+        return out
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("g++ not found (needed for the Python binding of musapy_b200)")
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-I", sysconfig.get_paths()["include"],
+           "-I", INCLUDE, src, "-o", out, "-L", LIBDIR, "-l:" + LIBNAME, "-Wl,-rpath,$ORIGIN"]
+    p = subprocess.run(cmd, capture_output=True, text=True)
+    if p.returncode != 0:
+        raise RuntimeError("Python binding build failed:\n" + p.stdout + p.stderr)
+    return out
 
 
 def main() -> None:

@@ -27,8 +27,8 @@ import torch
 from . import dtypes as _dt
 from . import errors
 from . import streams as _streams
-from ._lib import LIB, OPS, RED_OPS, check, i64arr
-from .array import Array, contiguous_strides, empty, parse_device, reshape
+from ._lib import LIB, NATIVE, OPS, RED_OPS, check, i64arr
+from .array import Array, _alloc, contiguous_strides, empty, parse_device, reshape
 
 _ARITH_OK = {_dt.F32, _dt.F64, _dt.C64, _dt.C128, _dt.F16, _dt.BF16}
 _UNARY_OK = {_dt.F32, _dt.F64, _dt.F16, _dt.BF16}
@@ -41,9 +41,7 @@ def _stream(dev: int) -> int:
 def _out(shape, d, dev: int) -> Array:
     """An op's result: device and dtype follow the inputs (input_array in
     musapy's resolution chain, resolution.rs:224-230)."""
-    res = empty(shape, d, dev)
-    res._dev_src = res._dt_src = "input_array"
-    return res
+    return _alloc(shape, d, dev, "input_array", "input_array")
 
 
 def _launch(op: str, dev: int, *arrays) -> int:
@@ -166,12 +164,9 @@ def _binary(name: str, a, b, out):
         res = out
     else:
         res = _out(shape, d, dev)
-    n = len(shape)
-    rc = LIB.mpb_elementwise(
-        OPS[name], n, i64arr(shape),
-        a.data_ptr, a.dtype.code, i64arr(_bstrides(a, shape)),
-        b.data_ptr, b.dtype.code, i64arr(_bstrides(b, shape)),
-        res.data_ptr, d.code, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
+    rc = NATIVE.elementwise(
+        OPS[name], shape, a.data_ptr, a.dtype.code, _bstrides(a, shape), b.data_ptr, b.dtype.code,
+        _bstrides(b, shape), res.data_ptr, d.code, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
     )
     check(rc, name)
     return res
@@ -213,11 +208,9 @@ def _compare(name: str, a, b, out):
         res = out
     else:
         res = _out(shape, _dt.bool_, dev)
-    rc = LIB.mpb_elementwise(
-        OPS[name], len(shape), i64arr(shape),
-        a.data_ptr, a.dtype.code, i64arr(_bstrides(a, shape)),
-        b.data_ptr, b.dtype.code, i64arr(_bstrides(b, shape)),
-        res.data_ptr, _dt.BOOL, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
+    rc = NATIVE.elementwise(
+        OPS[name], shape, a.data_ptr, a.dtype.code, _bstrides(a, shape), b.data_ptr, b.dtype.code,
+        _bstrides(b, shape), res.data_ptr, _dt.BOOL, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
     )
     check(rc, name)
     return res
@@ -267,9 +260,9 @@ def _unary(name: str, a: Array, out, p0: float = 0.0, p1: float = 0.0):
         res = out
     else:
         res = _out(a.shape, out_d, dev)
-    rc = LIB.mpb_elementwise(
-        OPS[name], a.ndim, i64arr(a.shape), a.data_ptr, d.code, i64arr(a.strides),
-        None, 0, None, res.data_ptr, out_d.code, d.code, float(p0), float(p1), _launch(name, dev, a, res),
+    rc = NATIVE.elementwise(
+        OPS[name], a._shape, a.data_ptr, d.code, a._strides, None, 0, None, res.data_ptr, out_d.code, d.code,
+        float(p0), float(p1), _launch(name, dev, a, res),
     )
     check(rc, name)
     return res
@@ -324,9 +317,9 @@ def _validate_cast(src: _dt.Dtype, dst: _dt.Dtype) -> None:
 def _cast_into(a: Array, d: _dt.Dtype, out: Array | None = None) -> Array:
     dev = a._dev
     res = out if out is not None else _out(a.shape, d, dev)
-    rc = LIB.mpb_elementwise(
-        OPS["cast"], a.ndim, i64arr(a.shape), a.data_ptr, a.dtype.code, i64arr(a.strides),
-        None, 0, None, res.data_ptr, d.code, d.code, 0.0, 0.0, _launch("cast", dev, a, res),
+    rc = NATIVE.elementwise(
+        OPS["cast"], a._shape, a.data_ptr, a.dtype.code, a._strides, None, 0, None, res.data_ptr, d.code, d.code,
+        0.0, 0.0, _launch("cast", dev, a, res),
     )
     check(rc, "cast")
     return res
@@ -453,9 +446,8 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
         if kernel in ("max", "min", "argmax", "argmin"):
             raise errors.ShapeError(f"{kernel}: zero-size reduction has no identity")
         fillv = {"sum": 0.0, "prod": 1.0, "mean": float("nan")}[kernel]
-        check(LIB.mpb_elementwise(OPS["fill"], len(out_shape), i64arr(out_shape), None, 0, None, None, 0, None,
-                                  res.data_ptr, out_d.code, out_d.code, fillv, 0.0, _launch("fill", dev, res)),
-              "fill")
+        check(NATIVE.elementwise(OPS["fill"], out_shape, None, 0, None, None, 0, None, res.data_ptr, out_d.code,
+                                 out_d.code, fillv, 0.0, _launch("fill", dev, res)), "fill")
         return res
     src = _widen_int(a)
     in_code = src.dtype.code
@@ -464,13 +456,12 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
     mask = 0
     for i in red:
         mask |= 1 << i
-    shape_c, strides_c = i64arr(src.shape), i64arr(src.strides)
     op = RED_OPS[kernel]
-    nbytes = LIB.mpb_reduce_scratch_bytes(op, src.ndim, shape_c, strides_c, src.data_ptr, in_code, mask, cd.code)
+    shape, strides, ptr = src._shape, src._strides, src.data_ptr
+    nbytes = NATIVE.reduce_scratch_bytes(op, shape, strides, ptr, in_code, mask, cd.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
-    rc = LIB.mpb_reduce(
-        op, src.ndim, shape_c, strides_c, src.data_ptr, in_code, mask,
-        res.data_ptr, out_d.code, cd.code, 1,
+    rc = NATIVE.reduce(
+        op, shape, strides, ptr, in_code, mask, res.data_ptr, out_d.code, cd.code, 1,
         scratch.data_ptr() if scratch is not None else None, nbytes, _launch(kernel, dev, src, res),
     )
     check(rc, kernel)
@@ -566,9 +557,8 @@ def set_scan_status_check(on: bool) -> None:
 def full(shape, fill_value, dtype=None, device=None) -> Array:
     res = empty(shape, dtype, device)
     v = complex(fill_value)
-    check(LIB.mpb_elementwise(OPS["fill"], res.ndim, i64arr(res.shape), None, 0, None, None, 0, None,
-                              res.data_ptr, res.dtype.code, res.dtype.code, v.real, v.imag,
-                              _launch("fill", res._dev, res)), "fill")
+    check(NATIVE.elementwise(OPS["fill"], res._shape, None, 0, None, None, 0, None, res.data_ptr, res.dtype.code,
+                             res.dtype.code, v.real, v.imag, _launch("fill", res._dev, res)), "fill")
     return res
 
 

@@ -60,6 +60,7 @@ class Stream:
         self._priority = int(priority)
         self._torch = _torch_stream if _torch_stream is not None else torch.cuda.Stream(
             device=f"cuda:{self._dev}", priority=self._priority)
+        self._handle = self._torch.cuda_stream
         self._id = next(_ids)
         self._poison = None
         self._ops = collections.deque(maxlen=OP_CONTEXT_DEPTH)
@@ -98,7 +99,7 @@ class Stream:
 
     @property
     def cuda_stream(self) -> int:
-        return self._torch.cuda_stream
+        return self._handle
 
     @property
     def torch_stream(self):
@@ -128,10 +129,10 @@ class Stream:
         self._ops.append(op)
 
     def __eq__(self, other) -> bool:
-        return isinstance(other, Stream) and other._dev == self._dev and other.cuda_stream == self.cuda_stream
+        return isinstance(other, Stream) and other._dev == self._dev and other._handle == self._handle
 
     def __hash__(self) -> int:
-        return hash((self._dev, self.cuda_stream))
+        return hash((self._dev, self._handle))
 
     def __repr__(self) -> str:
         return f"Stream(device=cuda:{self._dev}, priority={self._priority}, id={self._id})"
@@ -146,12 +147,25 @@ def _wrap(dev: int, ts) -> Stream:
     return s
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def current_stream(dev: int) -> Stream:
     """The stream ops on `dev` run on: the innermost ``ms.stream`` context for
     that device, else torch's current stream of the device (so torch stream
     contexts and CUDA graph capture are honoured)."""
-    for s in reversed(_stack("streams")):
-        if s._dev == dev:
+    st = getattr(_tls, "streams", None)
+    if st:
+        for s in reversed(st):
+            if s._dev == dev:
+                return s
+    if _raw_stream is not None and _wrappers:
+        # the handle alone is cheap; torch builds a Stream object per call
+        try:
+            s = _wrappers.get((dev, _raw_stream(dev)))
+        except RuntimeError:  # CUDA not usable: torch's own call raises below
+            s = None
+        if s is not None:
             return s
     return _wrap(dev, torch.cuda.current_stream(dev))
 
@@ -159,30 +173,35 @@ def current_stream(dev: int) -> Stream:
 def launch(op: str, dev: int, *arrays) -> int:
     """Prepare a launch of `op` on the current stream of `dev` touching
     `arrays` (inputs and outputs): poison check, cross-stream waits, allocator
-    stream bookkeeping, op context. Returns the CUDA stream handle."""
+    stream bookkeeping, op context. Returns the CUDA stream handle.
+
+    Each buffer remembers the Stream that last used it (`_mpb_stream`); the
+    Stream objects are unique per CUDA stream, so the common case - the same
+    stream again - is one identity test."""
     s = current_stream(dev)
     if s._poison is not None:
         raise errors.StreamError(s._poison)
-    ts = s._torch
     capturing = None
     for x in arrays:
         if x is None:
             continue
         buf = x._buf
         last = getattr(buf, "_mpb_stream", None)
-        if last is not None and last is not ts and last.cuda_stream != ts.cuda_stream:
+        if last is s:
+            continue
+        if last is not None and last._handle != s._handle:
             if capturing is None:
-                capturing = _capturing(ts)
+                capturing = _capturing(s._torch)
             if capturing:
                 # inside CUDA graph capture a wait on uncaptured work is not
                 # allowed; the capturing code orders its inputs beforehand
                 continue
-            ts.wait_stream(last)
-            buf.record_stream(ts)
+            s._torch.wait_stream(last._torch)
+            buf.record_stream(s._torch)
         if not capturing:
-            buf._mpb_stream = ts
-    s._note(op)
-    return ts.cuda_stream
+            buf._mpb_stream = s
+    s._ops.append(op)
+    return s._handle
 
 
 def _capturing(ts) -> bool:
@@ -197,9 +216,9 @@ def _capturing(ts) -> bool:
 def mark(dev: int, *arrays) -> None:
     """Record that `arrays` were just written on the current stream of `dev`
     by a torch operation (a copy), without waiting on anything."""
-    ts = current_stream(dev)._torch
+    s = current_stream(dev)
     for x in arrays:
-        x._buf._mpb_stream = ts
+        x._buf._mpb_stream = s
 
 
 # ----------------------------------------------------- context managers

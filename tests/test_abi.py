@@ -50,3 +50,26 @@ def test_version_and_promote_without_gpu():
 
     assert LIB.mpb_version() >= 1
     assert LIB.mpb_promote(4, 11, 0) == 11  # int64 + float64 -> float64
+
+
+def test_native_binding_shares_the_library_state():
+    """The compiled per-op binding calls the same loaded library as the
+    ctypes route: an error it raises is visible through mpb_last_error."""
+    from musapy_b200._lib import NATIVE, last_error
+
+    assert {"elementwise", "reduce", "reduce_scratch_bytes"} <= set(dir(NATIVE))
+    rc = NATIVE.elementwise(999, (4, 4), 16, 0, (4, 1), 32, 0, (4, 1), 48, 0, 0, 0.0, 0.0, 0)
+    assert rc != 0 and "unknown op 999" in last_error()
+
+
+def test_native_binding_validates_arguments():
+    from musapy_b200._lib import NATIVE
+
+    with pytest.raises(TypeError):
+        NATIVE.elementwise(0, (4,))
+    with pytest.raises(ValueError):
+        NATIVE.elementwise(0, (4, 4), 16, 0, (1,), 32, 0, (4, 1), 48, 0, 0, 0.0, 0.0, 0)
+    with pytest.raises(ValueError):
+        NATIVE.elementwise(0, (1,) * 33, 16, 0, None, None, 0, None, 48, 0, 0, 0.0, 0.0, 0)
+    with pytest.raises(TypeError):
+        NATIVE.reduce_scratch_bytes(0, (4,), (1,), 16, 0, "x", 0)
