@@ -231,14 +231,34 @@ int mpb_peer_close(void* peer_buf);
 int mpb_peer_free(void* buf);
 
 /* Exchange number `seq` (1, 2, ... the same sequence on every rank): stores
- * this rank's `rec_bytes` (16 or 32) record into every rank's buffer
+ * this rank's `rec_bytes` (8, 16, 24 or 32) record into every rank's buffer
  * (peers[r] is rank r's buffer as mapped here, peers[rank] the local one),
  * then waits until all `world` records of this exchange have arrived and
- * writes them to `out` in rank order (world x rec_bytes, 16-byte aligned).
- * Waits are bounded (~2 s): on expiry *status (device int) becomes
- * MPB_ERR_TIMEOUT and the kernel returns. At most 16 ranks. */
+ * writes them to `out` in rank order (world x rec_bytes, 8-byte aligned).
+ * Records travel as flag-in-line words (each 8-byte half of a 16-byte
+ * store is {4 data bytes, 32-bit seq}), so no fence or flag store is
+ * needed. Waits are bounded (~2 s): on expiry *status (device int) becomes
+ * MPB_ERR_TIMEOUT and the kernel returns without writing `out`. At most 16
+ * ranks. */
 int mpb_peer_allgather(const void* rec, int rec_bytes, void* const* peers, int rank, int world, uint64_t seq,
                        void* out, int* status, mpb_stream_t stream);
+
+/* The exchange of mpb_peer_allgather fused with the finish of a sharded
+ * sum: `partial` is this rank's f64 partial sum; the `world` partials are
+ * summed in rank order (the same value on every rank) and the sum and mean
+ * (over `count` elements) written in MPB_F32 or MPB_F64. One kernel. No
+ * counterpart in musapy. */
+int mpb_peer_sum_finalize(const double* partial, void* const* peers, int rank, int world, uint64_t seq, double count,
+                          int out_dtype, void* sum_out, void* mean_out, int* status, mpb_stream_t stream);
+
+/* The exchange fused with the finish of a sharded argmax / argmin: `record`
+ * is this rank's {value bits, local index} (MPB_R_ARG*_REC output); the
+ * records are combined in rank order as mpb_shard_arg_combine does
+ * (rank_offsets[r] = flat index of rank r's first element). One kernel. No
+ * counterpart in musapy. */
+int mpb_peer_arg_combine(const int64_t* record, void* const* peers, int rank, int world, uint64_t seq,
+                         const int64_t* rank_offsets, int is_max, int is_int, int64_t* out_index, double* out_value,
+                         int* status, mpb_stream_t stream);
 
 /* Sum of `world` f64 partials (stride_bytes apart) in rank order, then sum
  * and mean (over `count` elements) in MPB_F32 or MPB_F64. No counterpart in

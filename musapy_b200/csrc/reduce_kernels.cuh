@@ -32,6 +32,10 @@ template <class V>
 MPB_D ArgAcc<V> shfl_dn(ArgAcc<V> x, int o) {
   return ArgAcc<V>{shfl_dn(x.v, o), shfl_dn(x.i, o)};
 }
+MPB_D float shfl_x(float x, int o) { return __shfl_xor_sync(0xffffffffu, x, o); }
+MPB_D double shfl_x(double x, int o) { return __shfl_xor_sync(0xffffffffu, x, o); }
+MPB_D int64_t shfl_x(int64_t x, int o) { return __shfl_xor_sync(0xffffffffu, (long long)x, o); }
+MPB_D uint64_t shfl_x(uint64_t x, int o) { return __shfl_xor_sync(0xffffffffu, (unsigned long long)x, o); }
 
 MPB_D float radd(float a, float b) { return a + b; }
 MPB_D double radd(double a, double b) { return a + b; }
@@ -407,6 +411,24 @@ MPB_D void fold_segment_vec(typename P::Acc& acc, const typename P::In* __restri
     }
   }
   if constexpr (P::kArg) {
+    // Only a lane whose best equals the warp's best can hold the answer of
+    // the main loop's groups (a lower best is beaten by an element of the
+    // warp-best group); the other lanes skip the re-read, which on long
+    // segments is a DRAM access of four scattered 16-byte words per lane.
+    // Every caller runs this with the whole warp.
+    {
+      V wb = best;
+      bool wh = cbest >= 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const V ob = shfl_x(wb, o);
+        const bool oh = __shfl_xor_sync(0xffffffffu, (int)wh, o) != 0;
+        const bool t = oh && (!wh || P::beats(ob, wb));
+        wb = t ? ob : wb;
+        wh = wh || oh;
+      }
+      if (cbest >= 0 && !(best == wb)) cbest = -1;
+    }
     if (cbest >= 0) {
       // first element of the best group equal to the best value (it exists:
       // the group's extreme is one of its elements), merged with the rule

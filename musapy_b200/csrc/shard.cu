@@ -8,52 +8,21 @@
 #include <stdint.h>
 #include "common.cuh"
 #include "internal.h"
+#include "shard_combine.cuh"
 
 namespace mpb {
 namespace {
 
-constexpr int kMaxRanks = 64;
+constexpr int kMaxRanks = kShardMaxRanks;
 struct RankOffsets {
   int64_t off[kMaxRanks];
 };
 
-// recs: n records {value bits, local index} in rank order (all-gathered).
-// Rank 0 applies the first-element NaN rule, so a (NaN, 0) record from rank
-// 0 decides the answer; every other record never holds a NaN. Strict
-// comparison in rank order keeps the first occurrence.
+// recs: n all-gathered records {value bits, local index} in rank order.
 __global__ void k_arg_combine(const int64_t* __restrict__ recs, int n, RankOffsets ro, int is_max, int is_int,
                               int64_t* __restrict__ out_index, double* __restrict__ out_value) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int64_t best_i = INT64_MAX;
-  double best_d = 0.0;
-  int64_t best_v = 0;
-  bool have = false;
-  for (int r = 0; r < n; ++r) {
-    const int64_t vb = recs[2 * r], li = recs[2 * r + 1];
-    if (li == INT64_MAX) continue;
-    if (is_int) {
-      if (!have || (is_max ? vb > best_v : vb < best_v)) {
-        best_v = vb;
-        best_i = li + ro.off[r];
-        have = true;
-      }
-    } else {
-      const double v = __longlong_as_double(vb);
-      if (r == 0 && li == 0 && v != v) {  // NaN first element
-        best_d = v;
-        best_i = 0;
-        have = true;
-        break;
-      }
-      if (!have || (is_max ? v > best_d : v < best_d)) {
-        best_d = v;
-        best_i = li + ro.off[r];
-        have = true;
-      }
-    }
-  }
-  *out_index = have ? best_i : 0;
-  if (out_value) *out_value = is_int ? (double)best_v : best_d;
+  shard_arg_combine(recs, n, ro.off, is_max, is_int, out_index, out_value);
 }
 
 // Sum combine: `total` holds the all-reduced f64 sum; write the sum and the
@@ -61,15 +30,7 @@ __global__ void k_arg_combine(const int64_t* __restrict__ recs, int n, RankOffse
 __global__ void k_sum_finalize(const double* __restrict__ total, double count, int out_dt, void* sum_out,
                                void* mean_out) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const double t = *total;
-  const double m = t / count;
-  if (out_dt == MPB_F32) {
-    if (sum_out) *static_cast<float*>(sum_out) = __double2float_rn(t);
-    if (mean_out) *static_cast<float*>(mean_out) = __double2float_rn(m);
-  } else {
-    if (sum_out) *static_cast<double*>(sum_out) = t;
-    if (mean_out) *static_cast<double*>(mean_out) = m;
-  }
+  shard_sum_write(*total, count, out_dt, sum_out, mean_out);
 }
 
 }  // namespace

@@ -117,6 +117,22 @@ class PeerExchange:
         check(LIB.mpb_peer_allgather(rec.data_ptr(), rec.nbytes, self._ptrs, self.rank, self.world, self.seq,
                                      out.data_ptr(), self.status.data_ptr(), stream), "peer exchange")
 
+    def sum_finalize(self, partial: torch.Tensor, count: float, out_dtype: int, sum_ptr: int, mean_ptr: int,
+                     stream: int) -> None:
+        """Exchange the f64 partials and write the global sum and mean (one kernel)."""
+        self.seq += 1
+        check(LIB.mpb_peer_sum_finalize(partial.data_ptr(), self._ptrs, self.rank, self.world, self.seq, count,
+                                        out_dtype, sum_ptr, mean_ptr, self.status.data_ptr(), stream),
+              "peer exchange")
+
+    def arg_combine(self, rec: torch.Tensor, starts, is_max: bool, is_int: bool, index_ptr: int, value_ptr: int,
+                    stream: int) -> None:
+        """Exchange the (value, index) records and write the global index (one kernel)."""
+        self.seq += 1
+        check(LIB.mpb_peer_arg_combine(rec.data_ptr(), self._ptrs, self.rank, self.world, self.seq, i64arr(starts),
+                                       1 if is_max else 0, 1 if is_int else 0, index_ptr, value_ptr,
+                                       self.status.data_ptr(), stream), "peer exchange")
+
     def check(self) -> None:
         """Raise if any exchange gave up waiting for a rank (synchronises)."""
         if int(self.status.item()) != 0:
@@ -192,12 +208,11 @@ def sum_axis(x: ShardedArray, axis: int, out: Array | None = None) -> ShardedArr
 
 
 class _SumCombine:
-    """Scratch of a full sum/mean: the local partial (a 16-byte record for
-    the peer exchange), the gathered partials and the combined value."""
+    """Scratch of a full sum/mean: the local f64 partial (first of two
+    doubles: the NCCL route all-reduces it in place) and the results."""
 
     def __init__(self, dev: int, out_dt: _dt.Dtype, world: int = 1) -> None:
         self.partial = torch.zeros(2, dtype=torch.float64, device=f"cuda:{dev}")
-        self.parts = torch.zeros(2 * max(1, world), dtype=torch.float64, device=f"cuda:{dev}")
         self.sum_out = empty((), out_dt, dev)
         self.mean_out = empty((), out_dt, dev)
 
@@ -224,11 +239,8 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
     ex = peer_exchange(dev, x.group)
     if ex is not None:
         # partials of all ranks over NVLink, summed in rank order on every rank
-        if c.parts.numel() < 2 * world:
-            c.parts = torch.zeros(2 * world, dtype=torch.float64, device=f"cuda:{dev}")
-        ex.allgather(c.partial, c.parts[: 2 * world], stream)
-        check(LIB.mpb_shard_sum_parts_finalize(c.parts.data_ptr(), 16, world, float(x.global_size), a.dtype.code,
-                                               c.sum_out.data_ptr, c.mean_out.data_ptr, stream), "sum_all")
+        ex.sum_finalize(c.partial, float(x.global_size), a.dtype.code, c.sum_out.data_ptr, c.mean_out.data_ptr,
+                        stream)
         return c.sum_out, c.mean_out
     if world > 1:
         dist.all_reduce(c.partial, op=dist.ReduceOp.SUM, group=x.group)
@@ -265,13 +277,14 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
     check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
                          c.rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
                          scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
+    is_int = src.dtype.code in (_dt.I64, _dt.U64)
     ex = peer_exchange(dev, x.group)
     if ex is not None:
-        ex.allgather(c.rec, c.all, stream)
-        recs = c.all
         row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
         starts = [shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)]
-    elif world > 1:
+        ex.arg_combine(c.rec, starts, is_max, is_int, c.index.data_ptr, c.value.data_ptr(), stream)
+        return c.index
+    if world > 1:
         dist.all_gather_into_tensor(c.all, c.rec, group=x.group)
         recs = c.all
         row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
@@ -279,8 +292,7 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
     else:
         recs = c.rec
         starts = [0]
-    is_int = 1 if src.dtype.code in (_dt.I64, _dt.U64) else 0
-    check(LIB.mpb_shard_arg_combine(recs.data_ptr(), world, i64arr(starts), 1 if is_max else 0, is_int,
+    check(LIB.mpb_shard_arg_combine(recs.data_ptr(), world, i64arr(starts), 1 if is_max else 0, 1 if is_int else 0,
                                     c.index.data_ptr, c.value.data_ptr(), stream), "argreduce_all")
     return c.index
 
