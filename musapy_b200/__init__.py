@@ -56,6 +56,7 @@ from .errors import (
     DtypeError,
     InteropError,
     KernelError,
+    LinAlgError,
     MemoryError,
     MusapyError,
     OutOfMemoryError,

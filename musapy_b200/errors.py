@@ -43,3 +43,8 @@ class KernelError(MusapyError):
 
 class InteropError(MusapyError):
     pass
+
+
+class LinAlgError(MusapyError):
+    """Raised by musapy's linalg namespace; exported so that code catching
+    it keeps importing (linear algebra itself is not part of this engine)."""
