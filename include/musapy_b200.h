@@ -106,6 +106,21 @@ int mpb_elementwise(int op, int ndim, const int64_t* shape, const void* a, int a
                     const void* b, int b_dtype, const int64_t* b_strides, void* out, int out_dtype,
                     int compute_dtype, double p0, double p1, mpb_stream_t stream);
 
+/* Transposed-view elementwise ops (an input with unit stride on an outer
+ * dim) run through TMA tile loads when the view's layout allows it (16-byte
+ * aligned base and strides, 2-, 4- or 8-byte elements); mpb_ew_set_tma(0)
+ * routes them to the shared-memory tile kernel instead, (1) back, (-1)
+ * queries. Returns the previous setting. No counterpart in musapy. */
+int mpb_ew_set_tma(int enable);
+
+/* TMA-tiled kernel launches in this process so far. */
+uint64_t mpb_ew_tma_launches(void);
+
+/* Synchronous: *timed_out = 1 when a TMA tile wait gave up (2 s) since the
+ * last call on this device (the op's output is then incomplete), else 0;
+ * clears the flag. No counterpart in musapy. */
+int mpb_ew_wait_status(int* timed_out);
+
 /* -------------------------------------------------------------- reductions */
 
 /* Device scratch (bytes) mpb_reduce needs for this request; 0 when none. */

@@ -123,6 +123,11 @@ def _load() -> ctypes.CDLL:
     L.mpb_peer_allgather.restype = ctypes.c_int
     L.mpb_peer_allgather.argtypes = [c_vp, ctypes.c_int, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int,
                                      ctypes.c_uint64, c_vp, c_vp, c_vp]
+    L.mpb_ew_set_tma.restype = ctypes.c_int
+    L.mpb_ew_set_tma.argtypes = [ctypes.c_int]
+    L.mpb_ew_tma_launches.restype = ctypes.c_uint64
+    L.mpb_ew_wait_status.restype = ctypes.c_int
+    L.mpb_ew_wait_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.mpb_peer_sum_finalize.restype = ctypes.c_int
     L.mpb_peer_sum_finalize.argtypes = [c_vp, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
                                         ctypes.c_double, ctypes.c_int, c_vp, c_vp, c_vp, c_vp]

@@ -6,6 +6,7 @@
 #include <stdio.h>
 #include "elementwise.cuh"
 #include "internal.h"
+#include "tiled_tma.cuh"
 
 namespace mpb {
 namespace ew {
@@ -166,6 +167,16 @@ unsigned resident_grid(K kernel, int64_t items) {
   return (unsigned)(blocks < 1 ? 1 : blocks);
 }
 
+// TMA form with the second operand as the transposed one.
+template <class Op, class TC, class TA, class TB, class TO, int NIN>
+int run_tiled_tma_swapped(const Op& op, const TA* a, const TB* b, TO* out, const TiledArgs& t, cudaStream_t s) {
+  if constexpr (NIN == 2) {
+    return run_tiled_tma<Swapped<Op>, TC, TB, TA, TO, 2>(Swapped<Op>{op}, b, a, out, t, s);
+  } else {
+    return -1;
+  }
+}
+
 // Tile counts for an edge of `edge` elements.
 inline void tiled_count(TiledArgs& t, int edge) {
   t.ntp = cdiv(t.dp, edge);
@@ -209,6 +220,11 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
     case EW_TILED: {
       if constexpr (ALLOW_TILED) {
         TiledArgs t = tiled_args(g, NIN, pl.tiled_op, pl.tiled_p);
+        {
+          const int rc = pl.tiled_op == 0 ? run_tiled_tma<Op, TC, TA, TB, TO, NIN>(op, a, b, out, t, s)
+                                          : run_tiled_tma_swapped<Op, TC, TA, TB, TO, NIN>(op, a, b, out, t, s);
+          if (rc >= 0) return rc;
+        }
         tiled_count(t, tiled_edge<TC>());
         if (pl.tiled_op == 0) {
           auto k = k_ew_tiled<Op, TC, TA, TB, TO, NIN>;

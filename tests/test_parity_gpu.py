@@ -526,3 +526,66 @@ def test_python_scalar_operands(ms, oracle, dtype, scalar):
     got_r = ms.sub(scalar, xd).numpy()
     want_r = oracle.binary("sub", np.array(scalar, dtype=ms.dtypes.to_numpy(d)), x, all_gpu=True)
     assert_bits_equal(got_r, want_r, f"{scalar!r} - {dtype}")
+
+
+@pytest.fixture
+def tma_switch():
+    from musapy_b200._lib import LIB
+
+    prev = LIB.mpb_ew_set_tma(-1)
+    yield LIB
+    LIB.mpb_ew_set_tma(prev)
+
+
+@pytest.mark.parametrize("tma", [True, False])
+@pytest.mark.parametrize("dtype", [np.float16, np.float32, np.float64, np.int64, np.uint16])
+@pytest.mark.parametrize("shape", [(40, 104), (64, 256), (8, 4096), (1000, 8), (3, 40, 96), (2, 1000, 24),
+                                   (37, 100)])
+def test_tiled_tma_copies(ms, tma_switch, tma, dtype, shape):
+    """contiguous() of transposed views through the TMA tile kernel and the
+    shared-memory tile kernel: partial boxes along p and q, a batch dim,
+    2-, 4- and 8-byte elements, and a view whose strides rule TMA out."""
+    import ctypes
+
+    LIB = tma_switch
+    LIB.mpb_ew_set_tma(1 if tma else 0)
+    rng = np.random.default_rng(42)
+    x = rng.standard_normal(shape) * 1000
+    x = x.astype(dtype) if np.dtype(dtype).kind == "f" else rng.integers(-30000, 30000, shape).astype(dtype)
+    xd = dev(ms, x)
+    perm = tuple(range(x.ndim - 2)) + (x.ndim - 1, x.ndim - 2)
+    n0 = LIB.mpb_ew_tma_launches()
+    got = ms.contiguous(ms.transpose(xd, perm)).numpy()
+    assert_bits_equal(got, np.ascontiguousarray(np.transpose(x, perm)), f"transpose {shape}")
+    isz = np.dtype(dtype).itemsize
+    # the TMA kernel serves 2- and 8-byte elements (4-byte ones measured
+    # faster on the shared-memory tile kernel)
+    eligible = isz != 4 and (shape[-1] * isz) % 16 == 0 and shape[-2] % (16 // isz) == 0
+    assert (LIB.mpb_ew_tma_launches() > n0) == (tma and eligible), "TMA path taken iff enabled and eligible"
+    flag = ctypes.c_int(-1)
+    assert LIB.mpb_ew_wait_status(ctypes.byref(flag)) == 0 and flag.value == 0
+
+
+@pytest.mark.parametrize("tma", [True, False])
+def test_tiled_tma_binary(ms, oracle, tma_switch, tma):
+    """Binary ops with a transposed operand on both kernels: the other
+    operand a row (constant along p), a column or a full array, in both
+    operand orders, and musapy's int64-transposed + float64-row promotion."""
+    LIB = tma_switch
+    LIB.mpb_ew_set_tma(1 if tma else 0)
+    rng = np.random.default_rng(43)
+    a = rng.standard_normal((200, 136)).astype(np.float32)
+    at = ms.transpose(dev(ms, a))
+    ah = np.ascontiguousarray(a.T)
+    for other in (rng.standard_normal(200).astype(np.float32), rng.standard_normal((136, 1)).astype(np.float32),
+                  rng.standard_normal((136, 200)).astype(np.float32)):
+        od = dev(ms, other)
+        assert_bits_equal(ms.sub(at, od).numpy(), oracle.binary("sub", ah, other), "T - other")
+        assert_bits_equal(ms.div(od, at).numpy(), oracle.binary("div", other, ah), "other / T")
+    A = rng.integers(-1000, 1001, (96, 160), dtype=np.int64)
+    row = rng.standard_normal(96)
+    got = ms.add(ms.transpose(dev(ms, A)), dev(ms, row)).numpy()
+    want = oracle.binary("add", np.ascontiguousarray(A.T), row)
+    assert_bits_equal(got, want, "int64^T + float64 row")
+    got = ms.add(dev(ms, row), ms.transpose(dev(ms, A))).numpy()
+    assert_bits_equal(got, oracle.binary("add", row, np.ascontiguousarray(A.T)), "float64 row + int64^T")
