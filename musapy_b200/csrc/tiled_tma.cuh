@@ -224,6 +224,18 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
     const uint32_t tile = stages + (uint32_t)(s * TILE);
     const int64_t p0 = x.tp * PX + c * E, q0 = x.tq * kTmaRows;
     TO* ob = out + x.bi * t.bso;
+    // the other operand along q for every pass, loaded up front so that
+    // their latencies overlap (one wait per tile, not one per pass)
+    TC bq_all[NIN == 2 && BMODE == 1 ? PASSES : 1][E];
+    if constexpr (NIN == 2 && BMODE == 1) {
+      const TBv* bb = reinterpret_cast<const TBv*>(b) + x.bi * t.bsb;
+#pragma unroll
+      for (int pass = 0; pass < PASSES; ++pass) {
+        const int64_t q = q0 + (pass * RB + qb) * E;
+#pragma unroll
+        for (int k2 = 0; k2 < E; ++k2) bq_all[pass][k2] = q < t.dq ? cvt<TC>(bb[(q + k2) * t.sb_q]) : TC{};
+      }
+    }
 #pragma unroll
     for (int pass = 0; pass < PASSES; ++pass) {
       const int r0 = (pass * RB + qb) * E;
@@ -234,12 +246,6 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
       for (int k2 = 0; k2 < E; ++k2) {
         const int r = r0 + k2;
         v[k2] = lds128(tile + (uint32_t)(r * BOXB + c * 16));
-      }
-      TC bq[E];
-      if constexpr (NIN == 2 && BMODE == 1) {
-        const TBv* bb = reinterpret_cast<const TBv*>(b) + x.bi * t.bsb + q * t.sb_q;
-#pragma unroll
-        for (int k2 = 0; k2 < E; ++k2) bq[k2] = cvt<TC>(bb[k2 * t.sb_q]);
       }
 #pragma unroll
       for (int j = 0; j < E; ++j) {
@@ -252,7 +258,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
             if constexpr (NIN == 2) {
               TC bv;
               if constexpr (BMODE == 1) {
-                bv = bq[k2];
+                bv = bq_all[pass][k2];
               } else {
                 bv = cvt<TC>(reinterpret_cast<const TBv*>(b)[x.bi * t.bsb + p * t.sb_p + (q + k2) * t.sb_q]);
               }
