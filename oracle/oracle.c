@@ -424,10 +424,65 @@ static int64_t reduce_base(uint64_t out_idx, int ndim, const int64_t* shape, con
   return off;
 }
 
+/* One-output max/min/argmax/argmin over many threads with the sequential
+ * loop's exact result: chunk 0 runs the loop from element 0 (a NaN there
+ * decides, as x > NaN never holds); every later chunk finds the first
+ * occurrence of its largest (smallest) non-NaN element; the chunks are
+ * merged in order with the same strict comparison, so an equal value in a
+ * later chunk never replaces an earlier one. */
+#define OR_EXT_ALL(T, IS_NAN)                                                                  \
+  do {                                                                                        \
+    const T* x = (const T*)a + base;                                                          \
+    T cb[256];                                                                                \
+    int64_t ci[256];                                                                          \
+    int has[256];                                                                             \
+    _Pragma("omp parallel for schedule(static) num_threads(nch)")                             \
+    for (int t = 0; t < nch; ++t) {                                                           \
+      const int64_t k0 = axis_len * t / nch, k1 = axis_len * (t + 1) / nch;                  \
+      T best = x[0];                                                                          \
+      int64_t bi = 0;                                                                         \
+      int h = (t == 0);                                                                       \
+      for (int64_t k = (t == 0 ? 1 : k0); k < k1; ++k) {                                      \
+        const T v = x[k * ast];                                                               \
+        if (!h) {                                                                             \
+          if (!(IS_NAN(v))) { best = v; bi = k; h = 1; }                                      \
+        } else if ((want_max && v > best) || (!want_max && v < best)) {                       \
+          best = v; bi = k;                                                                   \
+        }                                                                                     \
+      }                                                                                       \
+      cb[t] = best; ci[t] = bi; has[t] = h;                                                   \
+    }                                                                                         \
+    T best = cb[0];                                                                           \
+    int64_t bi = ci[0];                                                                       \
+    for (int t = 1; t < nch; ++t)                                                             \
+      if (has[t] && ((want_max && cb[t] > best) || (!want_max && cb[t] < best))) {            \
+        best = cb[t]; bi = ci[t];                                                             \
+      }                                                                                       \
+    if (op == R_MAX || op == R_MIN) *(T*)c = best; else *(int64_t*)c = bi;                     \
+  } while (0)
+
+#define OR_NAN_F(v) ((v) != (v))
+#define OR_NAN_I(v) 0
+
+static int reduce_ext_all_parallel(int op, int dt, const void* a, void* c, int64_t base, int64_t ast,
+                                   int64_t axis_len) {
+  if (!(op == R_MAX || op == R_MIN || op == R_ARGMAX || op == R_ARGMIN)) return 0;
+  if (!(dt == F32 || dt == F64 || dt == I64) || g_threads <= 1 || axis_len < (1 << 16)) return 0;
+  const int want_max = (op == R_MAX || op == R_ARGMAX);
+  int nch = g_threads < 256 ? g_threads : 256;
+  if (dt == F32) OR_EXT_ALL(float, OR_NAN_F);
+  else if (dt == F64) OR_EXT_ALL(double, OR_NAN_F);
+  else OR_EXT_ALL(int64_t, OR_NAN_I);
+  return 1;
+}
+
 void or_reduce(int op, int dt, const void* a, void* c, int ndim, const int64_t* shape, const int64_t* strides,
                int axis, int64_t axis_len, int64_t out_size) {
   if (out_size <= 0 || axis_len <= 0) return;
   const int64_t ast = strides[axis];
+  if (out_size == 1 &&
+      reduce_ext_all_parallel(op, dt, a, c, reduce_base(0, ndim, shape, strides, axis), ast, axis_len))
+    return;
 #pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
   for (int64_t o = 0; o < out_size; ++o) {
     const int64_t base = reduce_base((uint64_t)o, ndim, shape, strides, axis);

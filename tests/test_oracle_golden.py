@@ -168,3 +168,42 @@ def test_python_broadcast_helpers_match_library():
             st = i64arr([0] * max(1, len(shape)))
             LIB.mpb_broadcast_strides(v.ndim, i64arr(v.shape), i64arr(v.strides), len(shape), i64arr(shape), st)
             assert list(ops._bstrides(v, shape)) == list(st[: len(shape)]), (v.shape, shape)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.int64])
+@pytest.mark.parametrize("op", ["max", "min", "argmax", "argmin"])
+def test_one_output_extremum_is_thread_count_independent(oracle, dtype, op):
+    """The oracle's chunked one-output extremum (several threads) gives the
+    sequential loop's exact result: first occurrence on ties, a NaN first
+    element decides, later NaNs are skipped, -0.0 and 0.0 compare equal."""
+    rng = np.random.default_rng(7)
+    n = 1 << 18
+    cases = []
+    if np.dtype(dtype).kind == "f":
+        x = rng.standard_normal(n).astype(dtype)
+        x[[5000, 90000, 200000]] = x.max() + 1  # ties across chunks
+        x[[7, 100000]] = np.nan
+        cases.append(x)
+        y = x.copy()
+        y[0] = np.nan
+        cases.append(y)
+        z = np.zeros(n, dtype)
+        z[:1000] = -0.0
+        z[150000] = 0.0
+        cases.append(z)
+        cases.append(np.full(n, np.nan, dtype))
+    else:
+        x = rng.integers(-50, 50, n).astype(dtype)
+        x[[3, 70000, 260000]] = 99
+        x[[4, 80000]] = -99
+        cases.append(x)
+    for x in cases:
+        for view in (x, x[::-1], x[1::3]):
+            try:
+                oracle.set_threads(1)
+                want = oracle.reduce(op, view, None)
+                oracle.set_threads(8)
+                got = oracle.reduce(op, view, None)
+            finally:
+                oracle.set_threads(1)
+            assert np.asarray(got).tobytes() == np.asarray(want).tobytes(), (op, dtype)
