@@ -6,13 +6,13 @@ of a global array; broadcast operands (a row vector) are replicated.
 
 * elementwise ops run on each shard independently (no communication);
 * reductions over non-leading axes stay local;
-* full reductions reduce the local shard on the GPU, move one 16-byte record
-  per rank over NVLink with ONE exchange - by default a peer-memory all-gather
-  kernel (PeerExchange: P2P stores into every rank's IPC-shared buffer and
-  bounded flag waits), or NCCL (all_reduce for sum/mean, all_gather for
-  argmax/argmin) with MUSAPY_B200_SHARD_COLLECTIVE=nccl - and finish on the
-  device with a one-thread combine in rank order, so no host round trip is
-  needed.
+* full reductions reduce the local shard on the GPU and move one 8- or
+  16-byte record per rank over NVLink with ONE exchange - by default a
+  peer-memory kernel (PeerExchange: P2P stores of flag-in-line words into
+  every rank's IPC-shared buffer, bounded waits) that also finishes the
+  reduction in rank order, or NCCL (all_reduce for sum/mean, all_gather for
+  argmax/argmin, then a one-thread device combine) with
+  MUSAPY_B200_SHARD_COLLECTIVE=nccl - so no host round trip is needed.
 
 The process group is torch.distributed's (backend "nccl" on GPUs, "gloo" in
 the CPU tests of the combine logic).
@@ -60,7 +60,8 @@ class ShardedArray:
 
 
 class PeerExchange:
-    """Small-record all-gather over NVLink peer memory (mpb_peer_allgather):
+    """Small-record exchange over NVLink peer memory (mpb_peer_allgather and
+    the fused mpb_peer_sum_finalize / mpb_peer_arg_combine):
     one exchange buffer per rank shared by CUDA IPC, one kernel per exchange,
     sequence numbers kept identical on all ranks by calling exchanges in the
     same order everywhere (as collectives already must be)."""
@@ -219,7 +220,8 @@ class _SumCombine:
 
 def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array, Array]:
     """Global sum and mean of a float array: local f32/f64 sum written as f64,
-    one all_reduce of 8 bytes, mean over the true global element count."""
+    one exchange of 8 bytes per rank (peer kernel with the finish fused, or
+    an NCCL all_reduce), mean over the true global element count."""
     a = x.local
     if a.dtype.code not in (_dt.F32, _dt.F64):
         raise errors.DtypeError("sum_all: float32/float64 shards only")
@@ -259,8 +261,9 @@ class _ArgCombine:
 
 def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | None = None) -> Array:
     """Global argmax/argmin (flat index, first occurrence, musapy's NaN rule):
-    local (value, index) record, one all_gather of 16 bytes per rank, device
-    combine in rank order."""
+    local (value, index) record, one exchange of 16 bytes per rank (peer
+    kernel with the combine fused, or an NCCL all_gather and a device
+    combine), in rank order."""
     a = x.local
     dev = a._dev
     world, rank = _world(x.group)
