@@ -501,8 +501,8 @@ def run_suite(args) -> None:
         return {"value": round(nb / sec / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                 "sample": desc, "ms": round(sec * 1e3, 2)}
 
-    def emit(cfg, op, nbytes, fn, note="", graph=False, cpu=None):
-        t, gbs, launches = timeit(fn, nbytes)
+    def emit(cfg, op, nbytes, fn, note="", graph=False, cpu=None, iters=None):
+        t, gbs, launches = timeit(fn, nbytes, iters)
         line = {"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1),
                 "frac": round(gbs / peak, 4), "bytes": int(nbytes), "launches": launches,
                 "peak": peak, "peak_kind": peak_kind, "note": note, "scale": args.scale}
@@ -522,9 +522,10 @@ def run_suite(args) -> None:
         ch = c.numpy()
         emit("C1", "add (4096,1)+(4096,)", 4096 * 4 * 2 + 4096 * 4096 * 4, lambda: ms.add(a, b, out=c),
              note="64 MB output: per-call host cost is a large part of ms; graph = kernels alone", graph=True,
-             cpu=(lambda: O.binary("add", d["a"], d["b"]), 4096 * 4 * 2 + 4096 * 4096 * 4, "whole op"))
+             cpu=(lambda: O.binary("add", d["a"], d["b"]), 4096 * 4 * 2 + 4096 * 4096 * 4, "whole op"),
+             iters=max(args.steps, 200))
         emit("C1", "sum axis=1", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r), graph=True,
-             cpu=(lambda: O.reduce("sum", ch, 1), 4096 * 4096 * 4 + 4096 * 4, "whole op"))
+             cpu=(lambda: O.reduce("sum", ch, 1), 4096 * 4096 * 4 + 4096 * 4, "whole op"), iters=max(args.steps, 200))
     if "C2" in cfgs:
         d = config_inputs("C2", args.scale)
         A, row, x = ms.from_numpy(d["A"]), ms.from_numpy(d["row"]), ms.from_numpy(d["x"])

@@ -137,7 +137,8 @@ def _prod(xs: Iterable[int]) -> int:
 class Array:
     """A strided view of device memory."""
 
-    __slots__ = ("_buf", "_shape", "_strides", "_offset", "_dtype", "_dev", "_name", "_dev_src", "_dt_src")
+    __slots__ = ("_buf", "_shape", "_strides", "_offset", "_dtype", "_dev", "_name", "_dev_src", "_dt_src", "_ptr",
+                 "_sid")
 
     def __init__(self, buf: torch.Tensor, shape, strides, offset: int, dtype: _dt.Dtype, device: int,
                  dev_src: str = "input_array", dt_src: str = "input_array") -> None:
@@ -150,6 +151,8 @@ class Array:
         self._name = None
         self._dev_src = dev_src  # how the device / dtype were resolved
         self._dt_src = dt_src
+        self._ptr = buf.data_ptr() + self._offset * dtype.itemsize  # device address of element [0, ..., 0]
+        self._sid = buf.untyped_storage().data_ptr()  # identity of the allocation (alias checks)
 
     # ------------------------------------------------------------ metadata
     @property
@@ -220,7 +223,7 @@ class Array:
     @property
     def data_ptr(self) -> int:
         """Device address of the logical element [0, ..., 0]."""
-        return self._buf.data_ptr() + self._offset * self._dtype.itemsize
+        return self._ptr
 
     def _stream(self) -> int:
         return _streams.current_stream(self._dev).cuda_stream
@@ -435,6 +438,7 @@ def _alloc(shape: tuple, d: _dt.Dtype, dev: int, dev_src: str, dt_src: str) -> A
     a._name = None
     a._dev_src = dev_src
     a._dt_src = dt_src
+    a._ptr = a._sid = buf.data_ptr()  # a fresh allocation starts its storage
     return a
 
 
@@ -539,7 +543,21 @@ def from_dlpack(obj) -> Array:
 
 # -------------------------------------------------------------------- views
 def _view(a: Array, shape, strides, offset) -> Array:
-    return Array(a._buf, shape, strides, offset, a._dtype, a._dev, a._dev_src, a._dt_src)
+    """A view of `a`'s allocation (shares its buffer, pointer base and
+    allocation identity)."""
+    v = _new_object(Array)
+    v._buf = a._buf
+    v._shape = tuple(int(x) for x in shape)
+    v._strides = tuple(int(x) for x in strides)
+    v._offset = int(offset)
+    v._dtype = a._dtype
+    v._dev = a._dev
+    v._name = None
+    v._dev_src = a._dev_src
+    v._dt_src = a._dt_src
+    v._ptr = a._ptr + (v._offset - a._offset) * a._dtype.itemsize
+    v._sid = a._sid
+    return v
 
 
 def transpose(a: Array, axes=None) -> Array:

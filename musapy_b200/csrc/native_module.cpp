@@ -14,6 +14,9 @@
 // Functions (all return the mpb status code; 0 = MPB_OK):
 //   elementwise(op, shape, a, a_dtype, a_strides, b, b_dtype, b_strides,
 //               out, out_dtype, compute_dtype, p0, p1, stream)
+//   elementwise_bc(op, out_shape, a, a_dtype, a_shape, a_strides, b,
+//                  b_dtype, b_shape, b_strides, out, out_dtype,
+//                  compute_dtype, p0, p1, stream)   (broadcast here)
 //   reduce_scratch_bytes(op, shape, strides, a, in_dtype, axes_mask,
 //                        compute_dtype) -> bytes
 //   reduce(op, shape, strides, a, in_dtype, axes_mask, out, out_dtype,
@@ -109,6 +112,65 @@ PyObject* py_elementwise(PyObject*, PyObject* const* args, Py_ssize_t n) {
   return PyLong_FromLong(rc);
 }
 
+// broadcast_strides (broadcast.rs:57-92): the strides of an operand of
+// shape in[0..ni) (strides st) on the output shape out[0..nd): 0 where a
+// dim is added on the left or stretched from extent 1.
+bool bcast_strides(const int64_t* out, int nd, const int64_t* in, const int64_t* st, int ni, int64_t* res) {
+  if (ni > nd) {
+    PyErr_SetString(PyExc_ValueError, "elementwise_bc: operand has more dims than the output");
+    return false;
+  }
+  for (int i = 0; i < nd; ++i) {
+    const int j = i - (nd - ni);
+    if (j < 0 || (in[j] == 1 && out[i] != 1)) {
+      res[i] = 0;
+    } else if (in[j] == out[i]) {
+      res[i] = st[j];
+    } else {
+      PyErr_Format(PyExc_ValueError, "elementwise_bc: extent %lld does not broadcast to %lld", (long long)in[j],
+                   (long long)out[i]);
+      return false;
+    }
+  }
+  return true;
+}
+
+// elementwise_bc(op, out_shape, a, a_dtype, a_shape, a_strides, b, b_dtype,
+//                b_shape, b_strides, out, out_dtype, compute_dtype, p0, p1,
+//                stream): a binary op with the operands' own shapes and
+// strides, broadcast here onto out_shape.
+PyObject* py_elementwise_bc(PyObject*, PyObject* const* args, Py_ssize_t n) {
+  if (!nargs(n, 16, "elementwise_bc")) return nullptr;
+  int op, a_dt, b_dt, out_dt, cdt;
+  int64_t shape[kMaxDims], ash[kMaxDims], ast[kMaxDims], bsh[kMaxDims], bst[kMaxDims];
+  int64_t as[kMaxDims], bs[kMaxDims];
+  void *a, *b, *out, *stream;
+  if (!i32(args[0], &op)) return nullptr;
+  const int nd = dims(args[1], shape, "out_shape");
+  if (nd < 0 || !ptr(args[2], &a) || !i32(args[3], &a_dt)) return nullptr;
+  const int na = dims(args[4], ash, "a_shape");
+  if (na < 0 || dims(args[5], ast, "a_strides") != na) {
+    if (!PyErr_Occurred()) PyErr_SetString(PyExc_ValueError, "elementwise_bc: a_strides and a_shape differ");
+    return nullptr;
+  }
+  if (!ptr(args[6], &b) || !i32(args[7], &b_dt)) return nullptr;
+  const int nb = dims(args[8], bsh, "b_shape");
+  if (nb < 0 || dims(args[9], bst, "b_strides") != nb) {
+    if (!PyErr_Occurred()) PyErr_SetString(PyExc_ValueError, "elementwise_bc: b_strides and b_shape differ");
+    return nullptr;
+  }
+  if (!ptr(args[10], &out) || !i32(args[11], &out_dt) || !i32(args[12], &cdt)) return nullptr;
+  const double p0 = PyFloat_AsDouble(args[13]);
+  if (p0 == -1.0 && PyErr_Occurred()) return nullptr;
+  const double p1 = PyFloat_AsDouble(args[14]);
+  if (p1 == -1.0 && PyErr_Occurred()) return nullptr;
+  if (!ptr(args[15], &stream)) return nullptr;
+  if (!bcast_strides(shape, nd, ash, ast, na, as) || !bcast_strides(shape, nd, bsh, bst, nb, bs)) return nullptr;
+  const int rc = mpb_elementwise(op, nd, shape, a, a_dt, as, b, b_dt, bs, out, out_dt, cdt, p0, p1,
+                                 (mpb_stream_t)stream);
+  return PyLong_FromLong(rc);
+}
+
 // shared head of the two reduce calls: op, shape, strides, a, in_dtype, mask
 struct RedHead {
   int op, nd, in_dt;
@@ -157,6 +219,8 @@ PyObject* py_reduce(PyObject*, PyObject* const* args, Py_ssize_t n) {
 PyMethodDef kMethods[] = {
     {"elementwise", (PyCFunction)(void (*)(void))py_elementwise, METH_FASTCALL,
      "mpb_elementwise with shapes and strides as tuples"},
+    {"elementwise_bc", (PyCFunction)(void (*)(void))py_elementwise_bc, METH_FASTCALL,
+     "mpb_elementwise of a binary op, broadcasting the operands' shapes and strides"},
     {"reduce_scratch_bytes", (PyCFunction)(void (*)(void))py_reduce_scratch_bytes, METH_FASTCALL,
      "mpb_reduce_scratch_bytes with shapes and strides as tuples"},
     {"reduce", (PyCFunction)(void (*)(void))py_reduce, METH_FASTCALL, "mpb_reduce with shapes and strides as tuples"},

@@ -123,9 +123,9 @@ def _bstrides(a: Array, shape) -> tuple:
 
 
 def _check_out(out: Array, shape, dtype: _dt.Dtype, dev: int, name: str) -> None:
-    if tuple(out.shape) != tuple(shape):
+    if out._shape != tuple(shape):
         raise errors.ShapeError(f"{name}: out shape {list(out.shape)} != expected {list(shape)}")
-    if out.dtype != dtype:
+    if out._dtype != dtype:
         raise errors.DtypeError(f"{name}: out dtype {out.dtype} != expected {dtype}")
     if out._dev != dev:
         raise errors.DeviceError(f"{name}: out device cuda:{out._dev} != input device cuda:{dev}")
@@ -134,7 +134,12 @@ def _check_out(out: Array, shape, dtype: _dt.Dtype, dev: int, name: str) -> None
 
 
 def _alias(out: Array, *ins: Array) -> bool:
-    return any(out._buf.untyped_storage().data_ptr() == x._buf.untyped_storage().data_ptr() for x in ins)
+    """musapy's AliasDetected rule: `out` shares its allocation with an input."""
+    sid = out._sid
+    for x in ins:
+        if x._sid == sid:
+            return True
+    return False
 
 
 def _same_device(name: str, *arrs: Array) -> int:
@@ -164,9 +169,9 @@ def _binary(name: str, a, b, out):
         res = out
     else:
         res = _out(shape, d, dev)
-    rc = NATIVE.elementwise(
-        OPS[name], shape, a.data_ptr, a.dtype.code, _bstrides(a, shape), b.data_ptr, b.dtype.code,
-        _bstrides(b, shape), res.data_ptr, d.code, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
+    rc = NATIVE.elementwise_bc(
+        OPS[name], shape, a._ptr, a._dtype.code, a._shape, a._strides, b._ptr, b._dtype.code, b._shape, b._strides,
+        res._ptr, d.code, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
     )
     check(rc, name)
     return res
@@ -208,9 +213,9 @@ def _compare(name: str, a, b, out):
         res = out
     else:
         res = _out(shape, _dt.bool_, dev)
-    rc = NATIVE.elementwise(
-        OPS[name], shape, a.data_ptr, a.dtype.code, _bstrides(a, shape), b.data_ptr, b.dtype.code,
-        _bstrides(b, shape), res.data_ptr, _dt.BOOL, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
+    rc = NATIVE.elementwise_bc(
+        OPS[name], shape, a._ptr, a._dtype.code, a._shape, a._strides, b._ptr, b._dtype.code, b._shape, b._strides,
+        res._ptr, _dt.BOOL, d.code, 0.0, 0.0, _launch(name, dev, a, b, res),
     )
     check(rc, name)
     return res

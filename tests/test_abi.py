@@ -73,3 +73,14 @@ def test_native_binding_validates_arguments():
         NATIVE.elementwise(0, (1,) * 33, 16, 0, None, None, 0, None, 48, 0, 0, 0.0, 0.0, 0)
     with pytest.raises(TypeError):
         NATIVE.reduce_scratch_bytes(0, (4,), (1,), 16, 0, "x", 0)
+
+
+def test_native_broadcast_binding_validates_shapes():
+    from musapy_b200._lib import NATIVE
+
+    with pytest.raises(ValueError):  # (3,) does not broadcast to (4,)
+        NATIVE.elementwise_bc(0, (4,), 16, 10, (3,), (1,), 32, 10, (4,), (1,), 48, 10, 10, 0.0, 0.0, 0)
+    with pytest.raises(ValueError):  # more dims than the output
+        NATIVE.elementwise_bc(0, (4,), 16, 10, (1, 4), (4, 1), 32, 10, (4,), (1,), 48, 10, 10, 0.0, 0.0, 0)
+    with pytest.raises(ValueError):  # strides and shape differ
+        NATIVE.elementwise_bc(0, (4,), 16, 10, (4,), (1, 1), 32, 10, (4,), (1,), 48, 10, 10, 0.0, 0.0, 0)
