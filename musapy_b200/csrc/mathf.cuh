@@ -254,10 +254,18 @@ MPB_D float sincos_wide(float x) {
   return __double2float_rn(COS ? cos((double)x) : sin((double)x));
 }
 
+// Arguments outside the fast range (|x| >= 2^15, inf, NaN): rare, so kept
+// out of line - inlined, their registers and stack (the double-precision
+// fallback) would be allocated in every elementwise loop that calls sin/cos.
+template <int COS>
+__device__ __noinline__ float sincos_slow(float x) {
+  return trig_in_range(x) ? sincos_core<COS>(x) : sincos_wide<COS>(x);
+}
+
 template <int COS>
 MPB_D float sincosf_(float x) {
   if (fabsf(x) < kTrigFastBound) return sincos_core_fast<COS>(x);  // false for NaN
-  return trig_in_range(x) ? sincos_core<COS>(x) : sincos_wide<COS>(x);
+  return sincos_slow<COS>(x);
 }
 // Two elements at once; a pair with an argument outside the fast range goes
 // element by element, so the results equal the one-element form's.
