@@ -608,3 +608,51 @@ def test_tiled_tma_sliced_views(ms, tma_switch, tma, dtype):
         want = np.ascontiguousarray(x[r0:r1, c0:c1].T)
         assert_bits_equal(ms.contiguous(view).numpy(), want, f"slice {(r0, c0, r1, c1)}")
         assert_bits_equal(ms.add(view, view).numpy(), (want.astype(np.float64) * 2).astype(dtype), "view + view")
+
+
+@pytest.mark.parametrize("shape", [(0,), (0, 5), (5, 0), (3, 0, 4)])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.int64, np.float16])
+def test_zero_size_every_family(ms, oracle, shape, dtype):
+    """Zero-size operands through every op family: results keep the
+    broadcast shape, empty reductions give the identity (sum 0, prod 1, mean
+    NaN as the CPU path divides 0 by a count of 0) or raise for max/min/
+    argmax/argmin, and cumsum, casts and transposed views stay empty."""
+    x = np.zeros(shape, dtype)
+    xd = dev(ms, x)
+    is_f = np.dtype(dtype).kind == "f"
+    if is_f:  # musapy's arithmetic whitelist is floating point
+        for name in ("add", "sub", "mul", "div", "pow"):
+            assert getattr(ms, name)(xd, xd).shape == shape, name
+            assert getattr(ms, name)(xd, dev(ms, np.ones(shape[-1:], dtype))).shape == shape, name + " broadcast"
+    for name in ("eq", "lt"):
+        r = getattr(ms, name)(xd, xd)
+        assert r.shape == shape and r.dtype == ms.bool_, name
+    if is_f:
+        for name in ("sin", "exp", "abs", "neg"):
+            assert getattr(ms, name)(xd).shape == shape, name
+        assert ms.clamp(xd, -1.0, 1.0).shape == shape
+    assert xd.astype("f64").shape == shape
+    assert ms.contiguous(ms.transpose(xd)).shape == tuple(reversed(shape))
+    if dtype == np.float16:  # musapy's cumsum takes integers, f32 and f64
+        with pytest.raises(ms.DtypeError):
+            ms.cumsum(xd)
+    else:
+        assert ms.cumsum(xd).shape == (0,)
+    for axis in range(len(shape)):
+        out_shape = shape[:axis] + shape[axis + 1:]
+        for name in ("sum", "prod", "mean"):
+            got = getattr(ms, name)(xd, axis=axis).numpy()
+            assert got.shape == out_shape, (name, axis)
+            if got.size and shape[axis] == 0:
+                want = {"sum": 0.0, "prod": 1.0, "mean": np.nan}[name]
+                np.testing.assert_array_equal(got.astype(np.float64), np.full(out_shape, want), err_msg=name)
+        for name in ("max", "argmax"):
+            if shape[axis] == 0:
+                with pytest.raises(ms.ShapeError):
+                    getattr(ms, name)(xd, axis=axis)
+            else:
+                assert getattr(ms, name)(xd, axis=axis).shape == out_shape
+    for name in ("max", "argmin"):
+        with pytest.raises(ms.ShapeError):
+            getattr(ms, name)(xd)
+    assert float(ms.sum(xd).numpy()) == 0.0 and float(ms.prod(xd).numpy()) == 1.0
