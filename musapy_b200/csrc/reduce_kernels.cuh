@@ -607,6 +607,8 @@ __global__ void __launch_bounds__(kRedThreads) k_red_col(const typename P::In* _
   }
 }
 
+constexpr int kCombineBatch = 8;
+
 // Combine S partials per output. layout 0: [M][S] (row splits, a warp per
 // output); layout 1: [S][M] (column splits, a thread per output). Partials
 // are merged in split order, so results do not depend on scheduling.
@@ -620,7 +622,19 @@ __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::I
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t o = gw; o < g.M; o += nw) {
       typename P::Acc acc = P::ident();
-      for (int j = lane; j < S; j += 32) acc = P::merge(acc, part[o * S + j]);
+      // kCombineBatch partials in flight per lane before they are merged, in
+      // the same order as one at a time (the loads do not wait on the merges)
+      for (int j0 = lane; j0 < S; j0 += 32 * kCombineBatch) {
+        typename P::Acc v[kCombineBatch];
+#pragma unroll
+        for (int u = 0; u < kCombineBatch; ++u) {
+          const int j = j0 + 32 * u;
+          if (j < S) v[u] = part[o * S + j];
+        }
+#pragma unroll
+        for (int u = 0; u < kCombineBatch; ++u)
+          if (j0 + 32 * u < S) acc = P::merge(acc, v[u]);
+      }
       acc = warp_reduce<P>(acc);
       const int64_t base = kept_off(g, o);
       acc = ext_zero_fix_warp<P>(acc, a + base, g, lane);
@@ -631,7 +645,15 @@ __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::I
     const int64_t gs = (int64_t)gridDim.x * blockDim.x;
     for (int64_t o = gt; o < g.M; o += gs) {
       typename P::Acc acc = part[o];
-      for (int j = 1; j < S; ++j) acc = P::merge(acc, part[(int64_t)j * g.M + o]);
+      for (int j0 = 1; j0 < S; j0 += kCombineBatch) {
+        typename P::Acc v[kCombineBatch];
+#pragma unroll
+        for (int u = 0; u < kCombineBatch; ++u)
+          if (j0 + u < S) v[u] = part[(int64_t)(j0 + u) * g.M + o];
+#pragma unroll
+        for (int u = 0; u < kCombineBatch; ++u)
+          if (j0 + u < S) acc = P::merge(acc, v[u]);
+      }
       const int64_t base = kept_off(g, o);
       write_out<P>(out, o, ext_zero_fix_thread<P>(acc, a + base, g), ro, a + base);
     }
