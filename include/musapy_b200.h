@@ -148,13 +148,18 @@ int mpb_reduce(int op, int ndim, const int64_t* shape, const int64_t* strides, c
  * exists for callers that cannot allocate device memory: an application that
  * embeds this library and owns the whole device budget through its own pool,
  * or a latency-critical loop in which cudaMalloc / cudaFree must not run
- * because they can synchronise the device. It allocates nothing. Requests
- * whose plan needs more than 256 KiB of scratch return MPB_ERR_SCRATCH (use
- * mpb_reduce for those). All calls on a GPU share the array and it keeps the
- * last call's contents (nothing in it needs to start at zero), so calls that
- * can overlap on the GPU race: order them on one stream or with events. The
- * first call on each device looks up the array's device address with that
- * device current; make that first call before any stream capture begins. */
+ * because they can synchronise the device. It allocates nothing. No request
+ * is refused for its size: the reduction splits across CTAs only as far as
+ * its partials fit in the 256 KiB (a reduction with more than 16384 outputs
+ * runs unsplit, which needs no scratch). Where that limit changes the split,
+ * float sums and means may differ from mpb_reduce's in the last bits;
+ * otherwise both run the same plan and agree bit for bit. All calls on a GPU
+ * share the array and it keeps the last call's contents (nothing in it needs
+ * to start at zero), so calls that can overlap on the GPU race: order them on
+ * one stream or with events. The first call on each device looks up the
+ * array's device address with that device current; make that first call
+ * before any stream capture begins (later uncaptured calls look it up again,
+ * so a device reset is picked up). */
 int mpb_reduce_noalloc(int op, int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype,
                        uint64_t axes_mask, void* out, int out_dtype, int compute_dtype, int nan_first_rule,
                        mpb_stream_t stream);
@@ -203,7 +208,8 @@ int mpb_eye(void* out, int dtype, int64_t rows, int64_t cols, int64_t k, mpb_str
 /* Copies `bytes` from pageable (or any) host memory to device memory `dst`
  * on `stream`, through a ring of pinned staging slots with the host-side
  * copies spread over a few threads and overlapped with the DMA of the
- * previous chunk. Returns once the host source has been read completely (it
+ * previous chunk; a page-locked source (cudaHostAlloc / cudaHostRegister) is
+ * moved by one DMA with no staging. Returns once the host source has been read completely (it
  * may be reused at once); the device copy completes in stream order. Replaces
  * the list-based host transfer of ms.array (rust/musapy-python/src/ops.rs:
  * 354-625) and the plain musaMemcpy behind it (musa_ffi.rs). The device is the
@@ -213,7 +219,7 @@ int mpb_copy_h2d(void* dst, const void* src, size_t bytes, mpb_stream_t stream);
 /* Copies `bytes` of device memory `src` to host memory `dst` after the work
  * already queued on `stream`, and returns when `dst` holds the data. Same
  * staging ring as mpb_copy_h2d, the DMA of chunk k+4 overlapping the host
- * copy of chunk k. Replaces Array.tolist's transfer (array.rs:451-488). */
+ * copy of chunk k; a page-locked destination gets one DMA, no staging. Replaces Array.tolist's transfer (array.rs:451-488). */
 int mpb_copy_d2h(void* dst, const void* src, size_t bytes, mpb_stream_t stream);
 
 /* ---------------------------------------------------- axis-0 sharding (new) */
@@ -274,6 +280,22 @@ int mpb_peer_sum_finalize(const double* partial, void* const* peers, int rank, i
 int mpb_peer_arg_combine(const int64_t* record, void* const* peers, int rank, int world, uint64_t seq,
                          const int64_t* rank_offsets, int is_max, int is_int, int64_t* out_index, double* out_value,
                          int* status, mpb_stream_t stream);
+
+/* The two fused exchanges above with all `world` ranks played on ONE GPU:
+ * one cooperative launch of `world` blocks (every block resident at once),
+ * block r acting as rank r with exchange buffer bufs[r] (zeroed
+ * mpb_peer_buffer_bytes() buffers on this GPU), record partials[r] /
+ * records[2r..2r+1] and results sum_out[r], mean_out[r] (f32 or f64 per
+ * out_dtype) / out_index[r], out_value[r]. The kernels, wire format, waits
+ * and combine are those of the per-rank calls; only the launch differs.
+ * For checking the multi-rank exchange and combine where fewer GPUs than
+ * ranks exist (ranks that wait on one another must never be separate
+ * launches on one GPU). No counterpart in musapy. */
+int mpb_peer_sum_finalize_emulated(const double* partials, void* const* bufs, int world, uint64_t seq, double count,
+                                   int out_dtype, void* sum_out, void* mean_out, int* status, mpb_stream_t stream);
+int mpb_peer_arg_combine_emulated(const int64_t* records, void* const* bufs, int world, uint64_t seq,
+                                  const int64_t* rank_offsets, int is_max, int is_int, int64_t* out_index,
+                                  double* out_value, int* status, mpb_stream_t stream);
 
 /* Sum of `world` f64 partials (stride_bytes apart) in rank order, then sum
  * and mean (over `count` elements) in MPB_F32 or MPB_F64. No counterpart in

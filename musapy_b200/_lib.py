@@ -134,6 +134,12 @@ def _load() -> ctypes.CDLL:
     L.mpb_peer_arg_combine.restype = ctypes.c_int
     L.mpb_peer_arg_combine.argtypes = [c_vp, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
                                        c_i64p, ctypes.c_int, ctypes.c_int, c_vp, c_vp, c_vp, c_vp]
+    L.mpb_peer_sum_finalize_emulated.restype = ctypes.c_int
+    L.mpb_peer_sum_finalize_emulated.argtypes = [c_vp, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_uint64,
+                                                 ctypes.c_double, ctypes.c_int, c_vp, c_vp, c_vp, c_vp]
+    L.mpb_peer_arg_combine_emulated.restype = ctypes.c_int
+    L.mpb_peer_arg_combine_emulated.argtypes = [c_vp, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_uint64, c_i64p,
+                                                ctypes.c_int, ctypes.c_int, c_vp, c_vp, c_vp, c_vp]
     L.mpb_shard_sum_parts_finalize.restype = ctypes.c_int
     L.mpb_shard_sum_parts_finalize.argtypes = [c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int,
                                                c_vp, c_vp, c_vp]

@@ -122,23 +122,37 @@ __global__ void k_peer_allgather(const uint32_t* __restrict__ rec, int words, Pe
   });
 }
 
+// The fused exchange kernels below run one rank per block: block b plays
+// rank `rank + b`, with its record at rec + b * (record words) and its
+// results at out + b. A rank's own launch has one block (b = 0: the rank,
+// record and outputs it was given). A launch of `world` blocks on one GPU,
+// cooperative so that every block is resident at once, plays all ranks of an
+// exchange over buffers of that GPU (mpb_peer_*_emulated): the same code,
+// protocol and combine, checkable without several GPUs.
+
 // Records are f64 partial sums (two words); summed in rank order, so every
 // rank computes the same value.
 __global__ void k_peer_sum_finalize(const uint32_t* __restrict__ partial, PeerPtrs peers, int rank, int world,
                                     unsigned long long seq, double count, int out_dt, void* sum_out, void* mean_out,
                                     int* status) {
-  exchange_then(partial, 2, peers, rank, world, seq, status, [&](const uint32_t* got) {
+  const int b = blockIdx.x;
+  const size_t osz = out_dt == MPB_F32 ? 4 : 8;
+  char* so = sum_out ? static_cast<char*>(sum_out) + b * osz : nullptr;
+  char* mo = mean_out ? static_cast<char*>(mean_out) + b * osz : nullptr;
+  exchange_then(partial + 2 * b, 2, peers, rank + b, world, seq, status, [&](const uint32_t* got) {
     double s = 0.0;
     for (int r = 0; r < world; ++r) s += __hiloint2double((int)got[2 * r + 1], (int)got[2 * r]);
-    shard_sum_write(s, count, out_dt, sum_out, mean_out);
+    shard_sum_write(s, count, out_dt, so, mo);
   });
 }
 
 __global__ void k_peer_arg_combine(const uint32_t* __restrict__ rec, PeerPtrs peers, int rank, int world,
                                    unsigned long long seq, PeerOffsets offs, int is_max, int is_int,
                                    int64_t* out_index, double* out_value, int* status) {
-  exchange_then(rec, 4, peers, rank, world, seq, status, [&](const uint32_t* got) {
-    shard_arg_combine(reinterpret_cast<const int64_t*>(got), world, offs.off, is_max, is_int, out_index, out_value);
+  const int b = blockIdx.x;
+  exchange_then(rec + 4 * b, 4, peers, rank + b, world, seq, status, [&](const uint32_t* got) {
+    shard_arg_combine(reinterpret_cast<const int64_t*>(got), world, offs.off, is_max, is_int, out_index + b,
+                      out_value ? out_value + b : nullptr);
   });
 }
 
@@ -257,6 +271,48 @@ int mpb_peer_arg_combine(const int64_t* record, void* const* peers, int rank, in
                                                          (unsigned long long)seq, po, is_max, is_int, out_index,
                                                          out_value, status);
   return launch_check("peer_arg_combine");
+}
+
+int mpb_peer_sum_finalize_emulated(const double* partials, void* const* bufs, int world, uint64_t seq, double count,
+                                   int out_dtype, void* sum_out, void* mean_out, int* status, mpb_stream_t stream) {
+  int rc = check_ranks("mpb_peer_sum_finalize_emulated", 0, world);
+  if (rc) return rc;
+  if (out_dtype != MPB_F32 && out_dtype != MPB_F64)
+    return fail(MPB_ERR_DTYPE, "mpb_peer_sum_finalize_emulated: output dtype must be f32 or f64");
+  if (!partials || !status) return fail(MPB_ERR_INVALID, "mpb_peer_sum_finalize_emulated: null pointer");
+  PeerPtrs pp{};
+  if ((rc = peer_ptrs("mpb_peer_sum_finalize_emulated", bufs, world, seq, pp))) return rc;
+  const uint32_t* rec = reinterpret_cast<const uint32_t*>(partials);
+  int rank0 = 0;
+  unsigned long long sq = (unsigned long long)seq;
+  void* args[] = {(void*)&rec, (void*)&pp, (void*)&rank0, (void*)&world, (void*)&sq, (void*)&count,
+                  (void*)&out_dtype, (void*)&sum_out, (void*)&mean_out, (void*)&status};
+  const cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_peer_sum_finalize, dim3(world), dim3(32), args, 0,
+                                                    (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_check(e, "peer_sum_finalize_emulated");
+  return launch_check("peer_sum_finalize_emulated");
+}
+
+int mpb_peer_arg_combine_emulated(const int64_t* records, void* const* bufs, int world, uint64_t seq,
+                                  const int64_t* rank_offsets, int is_max, int is_int, int64_t* out_index,
+                                  double* out_value, int* status, mpb_stream_t stream) {
+  int rc = check_ranks("mpb_peer_arg_combine_emulated", 0, world);
+  if (rc) return rc;
+  if (!records || !rank_offsets || !out_index || !status)
+    return fail(MPB_ERR_INVALID, "mpb_peer_arg_combine_emulated: null pointer");
+  PeerPtrs pp{};
+  if ((rc = peer_ptrs("mpb_peer_arg_combine_emulated", bufs, world, seq, pp))) return rc;
+  PeerOffsets po{};
+  for (int r = 0; r < world; ++r) po.off[r] = rank_offsets[r];
+  const uint32_t* rec = reinterpret_cast<const uint32_t*>(records);
+  int rank0 = 0;
+  unsigned long long sq = (unsigned long long)seq;
+  void* args[] = {(void*)&rec, (void*)&pp, (void*)&rank0, (void*)&world, (void*)&sq, (void*)&po,
+                  (void*)&is_max, (void*)&is_int, (void*)&out_index, (void*)&out_value, (void*)&status};
+  const cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_peer_arg_combine, dim3(world), dim3(32), args, 0,
+                                                    (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_check(e, "peer_arg_combine_emulated");
+  return launch_check("peer_arg_combine_emulated");
 }
 
 int mpb_shard_sum_parts_finalize(const double* parts, int stride_bytes, int world, double count, int out_dtype,

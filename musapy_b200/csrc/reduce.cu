@@ -164,7 +164,9 @@ int red_plan(const RedReq& r, RedPlan& pl) {
     if (R == 1 && pl.M < 2 * sms && pl.L >= 65536) {
       pl.kind = RK_ROW_SPLIT;
       int64_t S = cdiv(4 * sms, pl.M);
-      const int64_t max_s = pl.L / 16384;
+      int64_t max_s = pl.L / 16384;
+      if (r.scratch_cap > 0 && max_s > (int64_t)(r.scratch_cap / (16 * (size_t)pl.M)))
+        max_s = (int64_t)(r.scratch_cap / (16 * (size_t)pl.M));
       if (S > max_s) S = max_s;
       if (S < 1) S = 1;
       int64_t chunk = cdiv(pl.L, S);
@@ -194,6 +196,8 @@ int red_plan(const RedReq& r, RedPlan& pl) {
     const double data = (double)pl.M * (double)pl.L * (double)esz;
     int64_t s_max = pl.L / 64;
     if (s_max > 4096) s_max = 4096;
+    if (r.scratch_cap > 0 && s_max > (int64_t)(r.scratch_cap / (16 * (size_t)pl.M)))
+      s_max = (int64_t)(r.scratch_cap / (16 * (size_t)pl.M));
     int64_t best_s = 1;
     double best_cost = 0.0;
     for (int64_t S = 1; S <= (s_max > 1 ? s_max : 1); ++S) {

@@ -22,6 +22,7 @@ struct RedReq {
   void* scratch;
   size_t scratch_bytes;
   int allow_split;     // 0: never pick a plan that needs scratch
+  size_t scratch_cap;  // > 0: pick no split whose partials exceed this many bytes
   int64_t out_stride;  // elements between consecutive outputs (0 or 1: contiguous)
 };
 

@@ -2,8 +2,12 @@
 //
 // musapy has no multi-GPU code (docs/adr/ADR.md:896-906); these kernels are
 // the device-side halves of the new sharded path: after each rank reduces
-// its rows, the host moves one tiny record per rank with one NCCL collective
-// and these kernels finish on the device, so no host round trip is needed.
+// its rows, one tiny record per rank crosses to the other ranks and these
+// kernels finish on the device, so no host round trip is needed. They serve
+// the NCCL transport (MUSAPY_B200_SHARD_COLLECTIVE=nccl: an all_reduce or
+// all_gather moves the records, then one of these kernels combines them);
+// the default transport, the peer-memory exchange of peer.cu, fuses the
+// same combine (shard_combine.cuh) into its exchange kernel.
 #include <math.h>
 #include <stdint.h>
 #include "common.cuh"

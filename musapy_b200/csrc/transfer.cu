@@ -14,7 +14,10 @@
 // threads, which also spreads the first-touch page faults of a fresh
 // destination over several cores. One cudaMemcpyAsync per chunk; the ring
 // is a process-wide resource guarded by a mutex, so concurrent calls take
-// turns.
+// turns. Host memory that is already page-locked (cudaHostAlloc,
+// cudaHostRegister, torch's pin_memory) needs no staging: it is moved by one
+// DMA straight from or to the caller's buffer, and the call waits for that
+// DMA, so both kinds of host memory give the same return contract.
 #include <condition_variable>
 #include <cstring>
 #include <functional>
@@ -127,6 +130,7 @@ struct Ring {
   std::mutex mu;
   char* host = nullptr;                // kSlots * kSlotBytes pinned, portable
   cudaEvent_t ev[kMaxDevices][kSlots];  // per device: slot s free / filled
+  cudaEvent_t direct[kMaxDevices];      // per device: end of a direct DMA
   bool ev_made[kMaxDevices] = {false};
 };
 
@@ -149,12 +153,38 @@ int ring_ready(Ring& r, int dev) {
       int rc = cuda_check(cudaEventCreateWithFlags(&r.ev[dev][s], cudaEventDisableTiming), "copy: cudaEventCreate");
       if (rc != MPB_OK) return rc;
     }
+    int rc = cuda_check(cudaEventCreateWithFlags(&r.direct[dev], cudaEventDisableTiming), "copy: cudaEventCreate");
+    if (rc != MPB_OK) return rc;
     r.ev_made[dev] = true;
   }
   return MPB_OK;
 }
 
 int current_device(int* dev) { return cuda_check(cudaGetDevice(dev), "copy: cudaGetDevice"); }
+
+// True when both ends of [p, p + bytes) are page-locked host memory known to
+// CUDA. Pageable memory reports cudaMemoryTypeUnregistered (no error).
+bool page_locked(const void* p, size_t bytes) {
+  const char* ends[2] = {static_cast<const char*>(p), static_cast<const char*>(p) + bytes - 1};
+  for (const char* e : ends) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, e) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (a.type != cudaMemoryTypeHost) return false;
+  }
+  return true;
+}
+
+// One DMA between page-locked host memory and the device on `s`, then a wait
+// for it (lock held by the caller).
+int direct_copy(Ring& r, int dev, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind, cudaStream_t s) {
+  int rc = cuda_check(cudaMemcpyAsync(dst, src, bytes, kind, s), "copy: cudaMemcpyAsync (page-locked)");
+  if (rc != MPB_OK) return rc;
+  if ((rc = cuda_check(cudaEventRecord(r.direct[dev], s), "copy: cudaEventRecord")) != MPB_OK) return rc;
+  return cuda_check(cudaEventSynchronize(r.direct[dev]), "copy: page-locked DMA wait");
+}
 
 }  // namespace
 }  // namespace mpb
@@ -173,6 +203,7 @@ int mpb_copy_h2d(void* dst, const void* src, size_t bytes, mpb_stream_t stream) 
   Ring& r = ring();
   std::lock_guard<std::mutex> lk(r.mu);
   if ((rc = ring_ready(r, dev)) != MPB_OK) return rc;
+  if (page_locked(src, bytes)) return direct_copy(r, dev, dst, src, bytes, cudaMemcpyHostToDevice, s);
   // slots may still be read by DMAs of a previous call: wait per slot below
   const size_t nchunks = (bytes + kSlotBytes - 1) / kSlotBytes;
   for (size_t k = 0; k < nchunks; ++k) {
@@ -200,6 +231,7 @@ int mpb_copy_d2h(void* dst, const void* src, size_t bytes, mpb_stream_t stream) 
   Ring& r = ring();
   std::lock_guard<std::mutex> lk(r.mu);
   if ((rc = ring_ready(r, dev)) != MPB_OK) return rc;
+  if (page_locked(dst, bytes)) return direct_copy(r, dev, dst, src, bytes, cudaMemcpyDeviceToHost, s);
   const size_t nchunks = (bytes + kSlotBytes - 1) / kSlotBytes;
   auto issue = [&](size_t k) -> int {
     const int slot = (int)(k % kSlots);

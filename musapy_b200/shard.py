@@ -234,9 +234,13 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
     nbytes = LIB.mpb_reduce_scratch_bytes(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code,
                                           mask, cd.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
-    check(LIB.mpb_reduce(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code, mask,
-                         c.partial.data_ptr(), _dt.F64, cd.code, 1,
-                         scratch.data_ptr() if scratch is not None else None, nbytes, stream), "sum_all")
+    if a.size == 0:  # a rank without rows (more ranks than rows) contributes 0
+        with torch.cuda.stream(_streams.current_stream(dev).torch_stream):
+            c.partial.zero_()
+    else:
+        check(LIB.mpb_reduce(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code, mask,
+                             c.partial.data_ptr(), _dt.F64, cd.code, 1,
+                             scratch.data_ptr() if scratch is not None else None, nbytes, stream), "sum_all")
     world, _ = _world(x.group)
     ex = peer_exchange(dev, x.group)
     if ex is not None:
@@ -276,10 +280,15 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
     nbytes = LIB.mpb_reduce_scratch_bytes(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
                                           src.dtype.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
-    # only the shard holding global element 0 applies the first-element NaN rule
-    check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
-                         c.rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
-                         scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
+    if src.size == 0:  # a rank without rows sends the empty record {0, INT64_MAX}
+        with torch.cuda.stream(_streams.current_stream(dev).torch_stream):
+            c.rec[0] = 0
+            c.rec[1] = np.iinfo(np.int64).max
+    else:
+        # only the shard holding global element 0 applies the first-element NaN rule
+        check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
+                             c.rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
+                             scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
     is_int = src.dtype.code in (_dt.I64, _dt.U64)
     ex = peer_exchange(dev, x.group)
     if ex is not None:

@@ -47,3 +47,24 @@ def ms():
         # musapy has no implicit device (DeviceNotConfiguredError until one is set)
         ms.set_default_device("cuda:0")
     return ms
+
+
+# Full-size parity tests report how many output elements they compared with
+# the oracle; the counts are printed in pytest's terminal summary (also
+# under -q), one line per check.
+_COMPARED: list = []
+
+
+@pytest.fixture
+def compared(request):
+    def note(what: str, n: int) -> None:
+        _COMPARED.append((request.node.name, what, int(n)))
+    return note
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    if not _COMPARED:
+        return
+    terminalreporter.write_sep("-", "full-size parity: elements compared with the oracle")
+    for test, what, n in _COMPARED:
+        terminalreporter.write_line(f"{test}: {what}: {n:,} elements")

@@ -98,3 +98,37 @@ def assert_sum_close(got, want, absx_sum, rtol: float, what: str = "", truth=Non
         raise AssertionError(f"{what}: {int(bad.sum())} values outside rtol={rtol}*sum|x|; "
                              f"first: got {got.reshape(-1)[i]!r} want {want.reshape(-1)[i]!r} "
                              f"bound {np.broadcast_to(bound, got.shape).reshape(-1)[i]!r}")
+
+
+def bit_mismatches(got: np.ndarray, want: np.ndarray, chunk: int = 1 << 24) -> int:
+    """Number of elements whose bits differ between two same-shaped arrays of
+    one dtype, counted in chunks so that multi-GiB outputs need no large
+    temporaries. Two NaNs compare equal whatever their payloads."""
+    got, want = np.asarray(got), np.asarray(want)
+    assert got.shape == want.shape and got.dtype == want.dtype, (got.shape, want.shape, got.dtype, want.dtype)
+    g, w = got.reshape(-1), want.reshape(-1)
+    if got.dtype.kind == "c":
+        g, w = g.view(got.real.dtype), w.view(want.real.dtype)
+    floaty = _is_float_like(g.dtype)
+    bad = 0
+    for i in range(0, g.size, chunk):
+        gc, wc = g[i:i + chunk], w[i:i + chunk]
+        if floaty:
+            diff = bits(gc) != bits(wc)
+            if diff.any():
+                both_nan = np.isnan(gc.astype(np.float32)) & np.isnan(wc.astype(np.float32))
+                bad += int((diff & ~both_nan).sum())
+        else:
+            bad += int((gc != wc).sum())
+    return bad
+
+
+def max_ulp_chunked(got: np.ndarray, want: np.ndarray, chunk: int = 1 << 22) -> float:
+    """max ulp_diff over two large float arrays, chunk by chunk."""
+    g, w = np.asarray(got).reshape(-1), np.asarray(want).reshape(-1)
+    m = 0.0
+    for i in range(0, g.size, chunk):
+        d = ulp_diff(g[i:i + chunk], w[i:i + chunk])
+        if d.size:
+            m = max(m, float(d.max()))
+    return m

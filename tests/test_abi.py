@@ -3,7 +3,6 @@ function the public headers declare (no compute calls here)."""
 import ctypes
 import os
 import re
-import subprocess
 
 import pytest
 
@@ -34,15 +33,6 @@ def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(LIB_PATH)
     missing = [n for n in declared_functions() if not hasattr(lib, n)]
     assert not missing, f"declared but not exported: {missing[:20]}"
-
-
-def test_library_has_no_undefined_cuda_symbols_beyond_runtime():
-    from musapy_b200._lib import LIB_PATH
-
-    out = subprocess.run(["nm", "-D", "--undefined-only", LIB_PATH], capture_output=True, text=True).stdout
-    undefined = [l.split()[-1] for l in out.splitlines() if l.strip()]
-    forbidden = [u for u in undefined if "MemcpyBatch" in u or "Memcpy3DBatch" in u]
-    assert not forbidden
 
 
 def test_version_and_promote_without_gpu():

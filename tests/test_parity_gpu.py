@@ -38,7 +38,8 @@ def rand(rng, shape, dtype):
 
 # ------------------------------------------------------------- config 1
 def test_config1_broadcast_add_and_row_sum(ms, oracle):
-    """f32 (4096,1) + (4096,) from seed 0, then sum(axis=1)."""
+    """The CPU-runnable broadcast case: f32 (4096,1) + (4096,) drawn uniform[-1,1)
+    from numpy PCG64 seed 0, then sum(axis=1)."""
     rng = np.random.default_rng(0)
     a = rng.random((4096, 1), dtype=np.float32) * 2 - 1
     b = rng.random(4096, dtype=np.float32) * 2 - 1

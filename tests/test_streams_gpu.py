@@ -185,3 +185,26 @@ def test_resolution_sources_on_arrays(ms):
     t.start()
     t.join(30)
     assert out["dev"] == "cuda:0"
+
+
+@pytest.mark.parametrize("nbytes", [16, (1 << 20) + 3, (100 << 20) + 7])
+def test_page_locked_host_transfers_take_one_dma(ms, nbytes):
+    """mpb_copy_h2d / mpb_copy_d2h with page-locked host buffers (torch
+    pin_memory): one DMA each way, returning once the data has moved, so the
+    source can be overwritten at once and the destination read at once."""
+    import ctypes
+
+    import torch
+
+    from musapy_b200._lib import LIB
+
+    rng = np.random.default_rng(nbytes % 977)
+    src = torch.from_numpy(rng.integers(0, 256, nbytes, dtype=np.uint8)).pin_memory()
+    want = src.clone()
+    dev = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert LIB.mpb_copy_h2d(dev.data_ptr(), src.data_ptr(), nbytes, stream) == 0
+    src.zero_()  # the call returned: the DMA has read the source
+    dst = torch.zeros(nbytes, dtype=torch.uint8).pin_memory()
+    assert LIB.mpb_copy_d2h(dst.data_ptr(), dev.data_ptr(), nbytes, stream) == 0
+    assert torch.equal(dst, want)  # no synchronize needed: the call waited
