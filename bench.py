@@ -1,19 +1,29 @@
 """Benchmark: HBM GB/s of musapy's broadcast add and axis sums on B200.
 
-Workload: a float32 (65536, 32768) array, uniform[-1, 1)
-from numpy PCG64 seed 5, sharded on axis 0 across the GPUs of one node (one
-process per GPU), and a replicated (32768,) row vector drawn after it. One
-step is the hot path over the whole array:
+Workload: a float32 (65536, 32768) array, uniform[-1, 1) from numpy PCG64
+seed 5, sharded on axis 0 across the GPUs of one node (one process per GPU),
+and a replicated (32768,) row vector drawn after it. One step is the hot
+path over the whole array:
 
     y   = x + row                 broadcast add           (local)
     r   = sum(y, axis=1)          axis sum                (local)
-    s,m = sum(x), mean(x)         full reduction          (one NCCL all_reduce)
-    i   = argmax(x)               full arg reduction      (one NCCL all_gather)
+    s,m = sum(x), mean(x)         full reduction          (8-byte record per rank)
+    i   = argmax(x)               full arg reduction      (16-byte record per rank)
+
+With several ranks each full reduction ends with one record exchange over
+NVLink: the peer-memory exchange kernel (csrc/peer.cu) stores the rank's
+record into every peer's buffer and finishes the reduction in the same
+kernel (NCCL collectives with MUSAPY_B200_SHARD_COLLECTIVE=nccl).
 
 `value` = algorithmic bytes of all ranks / step time (each input read once,
 each output written once), max over ranks; `e2e` is the same metric with the
-step's input copied from pinned host memory and its results copied back
-inside the timed region. Total work is fixed as N grows (strong scaling).
+step's input copied from pinned host memory through the library's transfer
+entry points (mpb_copy_h2d / mpb_copy_d2h) and its results copied back inside
+the timed region. Total work is fixed as N grows (strong scaling). At one GPU
+the line also carries `config.suite`: every op of the other workloads of the
+benchmark set (the CPU-runnable broadcast add, the mixed-dtype strided and
+transcendental chain, the 3-D reductions and cumsums, the low-precision and
+complex elementwise ops), timed through the API in the same run.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -76,6 +86,46 @@ def gen_row_vector(rows: int, cols: int):
     return np.random.Generator(bg).random(cols, dtype=np.float32) * 2 - 1
 
 
+def gen_rows_parallel(r0: int, r1: int, cols: int, out, threads: int = 0):
+    """gen_rows over several host threads: each block of rows advances its
+    own copy of the stream, so the result is the same matrix."""
+    import concurrent.futures as cf
+
+    threads = threads or min(32, os.cpu_count() or 1)
+    n = r1 - r0
+    per = max(1, -(-n // (threads * 4)))
+    jobs = [(r0 + i, min(r1, r0 + i + per)) for i in range(0, n, per)]
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda j: gen_rows(j[0], j[1], cols, out=out[j[0] - r0:j[1] - r0]), jobs))
+    return out
+
+
+def host_info() -> dict:
+    """The GPU box's host: logical CPUs, the CPUs this process may run on,
+    the CPU model and the memory available."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except Exception:
+        usable = os.cpu_count()
+    mem = None
+    try:
+        import psutil
+
+        mem = round(psutil.virtual_memory().available / 2**30, 1)
+    except Exception:
+        pass
+    return {"nproc": os.cpu_count(), "usable_cpus": usable, "cpu_model": model, "mem_available_gib": mem}
+
+
 def step_bytes(rows: int, cols: int) -> dict:
     n = rows * cols * 4
     return {
@@ -96,15 +146,31 @@ def measured_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def ncu_traffic() -> dict:
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
-    summary, if one exists (profiles/ncu_traffic.json)."""
+def add_traffic(rows: int):
+    """DRAM bytes (read + write) of one broadcast-add launch over `rows` rows,
+    from the committed ncu captures (profiles/ncu_traffic.json): a capture of
+    that very launch size when there is one, else the line through captures
+    at two sizes (slope per row + a constant part, e.g. output still dirty in
+    L2 when the kernel ends). Returns (bytes or None, how)."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(p) as f:
-            return json.load(f)
+            caps = json.load(f).get("captures", [])
     except Exception:
-        return {}
+        return None, "no capture"
+    pts = {}
+    for c in caps:
+        try:
+            pts[int(c["rows"])] = int(c["dram_bytes_read"]) + int(c["dram_bytes_write"])
+        except (KeyError, TypeError, ValueError):
+            continue
+    if rows in pts:
+        return pts[rows], f"ncu capture of this launch ({rows} rows)"
+    if len(pts) >= 2:
+        (r0, b0), (r1, b1) = sorted(pts.items())[-2:]
+        slope = (b1 - b0) / (r1 - r0)
+        return int(round(b0 + slope * (rows - r0))), f"line through ncu captures at {r0} and {r1} rows"
+    return None, "fewer than two captures"
 
 
 class ClockSampler:
@@ -188,29 +254,65 @@ def cpu_sample(rows: int, cols: int, threads: int, steps: int, warmup: int) -> d
     dt = (time.perf_counter() - t0) / steps
     total = sum(b.values())
     return {"value": total / dt / 1e9, "unit": "GB/s", "cores": threads, "seconds_per_step": dt,
+            "host": host_info(),
             "sample": f"first {rows} of {ROWS} rows ({rows * cols} f32 elements), same step, "
                       f"{'1 thread (scalar port)' if threads == 1 else f'{threads} OpenMP threads'}"}
 
 
 def run_reference(args) -> None:
+    """The reference CPU path of the step (the oracle port: musapy's CPU loops
+    restated, each output computed in the reference's order; all host
+    threads) on the full workload when the host has the memory for it (x and
+    y, 16 GiB), else on the first --sample-rows rows. Warm-up steps run on a
+    2048-row slice (they only warm the threads and the allocator)."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return
+    import numpy as np
+
     from oracle import oracle as O
 
     O.build()
     threads = O.max_threads()
-    rows = args.sample_rows
-    r = cpu_sample(rows, COLS, threads, max(1, args.steps), max(0, args.warmup))
+    O.set_threads(threads)
+    host = host_info()
+    need_gib = 2 * ROWS * COLS * 4 / 2**30 + 2
+    full = host["mem_available_gib"] is None or host["mem_available_gib"] > need_gib + 8
+    rows = ROWS if full else args.sample_rows
+    x = np.empty((rows, COLS), dtype=np.float32)
+    gen_rows_parallel(0, rows, COLS, x)
+    row = gen_row_vector(ROWS, COLS)
+    y = np.empty_like(x)
+    y.fill(0.0)  # first-touch page faults outside the timed steps
+
+    def one(xs, ys):
+        O.binary("add", xs, row, out=ys)
+        O.reduce("sum", ys, axis=1)
+        O.reduce("sum", xs, None)
+        O.reduce("mean", xs, None)
+        O.reduce("argmax", xs, None)
+
+    for _ in range(max(0, args.warmup)):
+        one(x[:2048], y[:2048])
+    steps = max(1, args.steps)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one(x, y)
+    dt = (time.perf_counter() - t0) / steps
+    value = sum(step_bytes(rows, COLS).values()) / dt / 1e9
+    sample = (f"the full workload ({rows} x {COLS} f32), same step" if full else
+              f"first {rows} of {ROWS} rows (host memory {host['mem_available_gib']} GiB < the {need_gib:.0f} GiB "
+              f"the full workload needs)")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(r["seconds_per_step"] * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "rows_sampled": rows, "cols": COLS},
-        "cpu_baseline": {"value": round(r["value"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": r["sample"]},
-        "e2e": {"value": round(r["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": WORKLOAD, "rows": rows, "cols": COLS, "same_config": full,
+                   "warmup_sample": "warm-up steps on the first 2048 rows"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample + f", {threads} OpenMP threads", "host": host},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -307,31 +409,40 @@ def run_b200(args) -> None:
              for i, name in enumerate(["add", "sum_axis1", "sum_all", "argmax"])}
     clk = clocks.stop(set(range(world))) if local == 0 else None
 
-    # e2e through the public API: host input -> device, step, results -> host
+    # e2e through the library's own transfer entry points: the step's input
+    # from pinned host memory to the device (mpb_copy_h2d: one DMA for
+    # page-locked memory), the step, the results back (mpb_copy_d2h); both
+    # calls return once their copy is done
+    from musapy_b200._lib import LIB, check
+
     host_rowsum = torch.empty((nloc,), dtype=torch.float32, pin_memory=True)
     # one pinned buffer per result in the result's own dtype: a plain D2H copy,
     # no conversion kernel on the device
     host_sum = torch.empty(1, dtype=sc.sum_out.torch().dtype, pin_memory=True)
     host_mean = torch.empty(1, dtype=sc.mean_out.torch().dtype, pin_memory=True)
     host_index = torch.empty(1, dtype=ac.index.torch().dtype, pin_memory=True)
+    sraw = stream.cuda_stream
+    copies_in = [(x.data_ptr, host_x.data_ptr(), host_x.nbytes), (row.data_ptr, host_row.data_ptr(), host_row.nbytes)]
+    copies_out = [(host_rowsum.data_ptr(), rowsum.data_ptr, host_rowsum.nbytes),
+                  (host_sum.data_ptr(), sc.sum_out.data_ptr, host_sum.nbytes),
+                  (host_mean.data_ptr(), sc.mean_out.data_ptr, host_mean.nbytes),
+                  (host_index.data_ptr(), ac.index.data_ptr, host_index.nbytes)]
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e2e_steps):
-        x.torch().copy_(host_x, non_blocking=True)
-        row.torch().copy_(host_row, non_blocking=True)
+        for d, h, n in copies_in:
+            check(LIB.mpb_copy_h2d(d, h, n, sraw), "e2e input copy")
         step()
-        host_rowsum.copy_(rowsum.torch(), non_blocking=True)
-        host_sum.copy_(sc.sum_out.torch().reshape(1), non_blocking=True)
-        host_mean.copy_(sc.mean_out.torch().reshape(1), non_blocking=True)
-        host_index.copy_(ac.index.torch().reshape(1), non_blocking=True)
+        for h, d, n in copies_out:
+            check(LIB.mpb_copy_d2h(h, d, n, sraw), "e2e result copy")
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    h2d = nloc * cols * 4 + cols * 4
-    d2h = host_rowsum.nbytes + host_sum.nbytes + host_mean.nbytes + host_index.nbytes
+    h2d = sum(n for _, _, n in copies_in)
+    d2h = sum(n for _, _, n in copies_out)
 
     # max over ranks of the step time, total bytes over ranks
     b_local = step_bytes(nloc, cols)
@@ -346,10 +457,19 @@ def run_b200(args) -> None:
     peak, peak_kind = measured_peak()
     add_bytes = b_local["add"]
     achieved = add_bytes / (op_ms["add"] * 1e-3) / 1e9
-    tr = ncu_traffic()
-    traffic = None
-    if tr.get("kernel_bytes_per_launch") and tr.get("rows_per_launch"):
-        traffic = int(tr["kernel_bytes_per_launch"] * (nloc / tr["rows_per_launch"]))
+    traffic, traffic_how = add_traffic(nloc)
+
+    suite = None
+    if world == 1 and not args.no_suite:
+        del x, y, xs, ys, host_x
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        clocks_s = ClockSampler()
+        clocks_s.start()
+        time.sleep(0.3)
+        suite = {"ops": device_suite(args, peak), "inputs": SUITE_INPUTS}
+        torch.cuda.synchronize()
+        suite["clocks"] = clocks_s.stop({local})
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -375,15 +495,17 @@ def run_b200(args) -> None:
                    "per_op_frac": {k: round(b_local[k] / (v * 1e-3) / 1e9 / peak, 4) for k, v in op_ms.items()}},
         "roofline": {"bound": "hbm", "kernel": "k_ew_rows (broadcast add)", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "bytes_per_launch": add_bytes, "traffic": traffic},
+                     "bytes_per_launch": add_bytes, "traffic": traffic, "traffic_source": traffic_how},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
                 "d2h_bytes_per_step": d2h * world, "ms_per_step": round(t_e2e, 3)},
         "gpu_launches": int(launches),
         "clocks": clk,
     }
+    if suite is not None:
+        line["config"]["suite"] = suite
     if cpu is not None:
         line["cpu_baseline"] = {"value": round(cpu["value"], 4), "unit": "GB/s", "cores": cpu["cores"],
-                                "kind": "port", "sample": cpu["sample"]}
+                                "kind": "port", "sample": cpu["sample"], "host": cpu["host"]}
     print(json.dumps(line), flush=True)
 
 
@@ -649,6 +771,177 @@ def run_suite(args) -> None:
     torch.cuda.empty_cache()
 
 
+SUITE_INPUTS = ("the CPU-runnable broadcast add from its numpy seed; the other workloads' inputs drawn on the "
+                "device by torch's seeded generator with the same shapes, dtypes and value distributions as their "
+                "numpy-seeded versions (the parity tests check those): N(0,1), uniform ints in [-1000, 1000], "
+                "uniform[0.1,4) and uniform[-2,2) f16, complex64 with N(0,1) parts. CUDA events over back-to-back "
+                "API calls after warm-up; every input except the broadcast add's is larger than the L2; that one "
+                "(64 MB) is also replayed from a CUDA graph, which drops the per-call host cost")
+
+
+def device_suite(args, peak: float) -> list:
+    """Every op of the benchmark set's other workloads, timed through the
+    public API on the current GPU (ms per call, GB/s of algorithmic bytes,
+    fraction of the measured HBM peak)."""
+    import numpy as np
+    import torch
+
+    import musapy_b200 as ms
+
+    stream = torch.cuda.current_stream()
+    iters = max(10, args.steps)
+    out = []
+
+    def timeit(fn, n):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = ms._lib.launch_count()
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n, (ms._lib.launch_count() - l0) // n
+
+    def graph_ms(fn, reps=20):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                fn()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / (iters * reps)
+
+    def emit(cfg, op, nbytes, fn, n=None, graph=False):
+        t, launches = timeit(fn, n or iters)
+        gbs = nbytes / (t * 1e-3) / 1e9
+        e = {"config": cfg, "op": op, "ms": round(t, 4), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+             "bytes": int(nbytes), "launches": launches}
+        if graph:
+            tg = graph_ms(fn)
+            gg = nbytes / (tg * 1e-3) / 1e9
+            e["graph"] = {"ms": round(tg, 4), "gbs": round(gg, 1), "frac": round(gg / peak, 4)}
+        out.append(e)
+
+    def dev(shape, dtype):
+        a = ms.empty(shape, dtype)
+        return a, a.torch()
+
+    gen = torch.Generator(device="cuda")
+
+    # C1: (4096,1) + (4096,) f32 from numpy seed 0, then sum(axis=1)
+    d = config_inputs("C1")
+    a, b = ms.from_numpy(d["a"]), ms.from_numpy(d["b"])
+    c = ms.add(a, b)
+    r = ms.sum(c, axis=1)
+    emit("C1", "add (4096,1)+(4096,) f32", 4096 * 8 + 4096 * 4096 * 4, lambda: ms.add(a, b, out=c), n=200,
+         graph=True)
+    emit("C1", "sum axis=1 (4096,4096) f32", 4096 * 4096 * 4 + 4096 * 4, lambda: ms.sum(c, axis=1, out=r), n=200,
+         graph=True)
+    del a, b, c, r
+
+    # C2: int64 (8192,8192) read transposed + f64 row; f32 chain on 2^28
+    gen.manual_seed(2)
+    A, At_ = dev((8192, 8192), "i64")
+    At_.random_(-1000, 1001, generator=gen)
+    row, rt = dev((8192,), "f64")
+    rt.normal_(generator=gen)
+    x, xt = dev((1 << 28,), "f32")
+    xt.normal_(generator=gen)
+    AT = ms.transpose(A)
+    o = ms.add(AT, row)
+    emit("C2", "add int64^T (8192,8192) + f64 row -> f64", 8192 * 8192 * 16 + 8192 * 8, lambda: ms.add(AT, row, out=o))
+    s_ = ms.sin(x)
+    e_ = ms.exp(s_)
+    cl = ms.clamp(e_, -0.5, 0.5)
+    n = 1 << 28
+    emit("C2", "sin f32 2^28", n * 8, lambda: ms.sin(x, out=s_))
+    emit("C2", "exp f32 2^28", n * 8, lambda: ms.exp(s_, out=e_))
+    emit("C2", "clamp f32 2^28", n * 8, lambda: ms.clamp(e_, -0.5, 0.5, out=cl))
+    del A, At_, row, rt, x, xt, AT, o, s_, e_, cl
+
+    # C3: f32 (64,4096,4096) N(0,1)
+    gen.manual_seed(1)
+    x, xt = dev((64, 4096, 4096), "f32")
+    xt.normal_(generator=gen)
+    nb = 64 * 4096 * 4096 * 4
+    for axis, outs in ((2, 64 * 4096), (0, 4096 * 4096), ((0, 2), 4096)):
+        for op in ("sum", "max", "mean"):
+            f = getattr(ms, op)
+            res = f(x, axis=axis)
+            emit("C3", f"{op} axis={axis}", nb + outs * 4, lambda f=f, axis=axis, res=res: f(x, axis=axis, out=res))
+    am = ms.argmax(x, axis=1)
+    emit("C3", "argmax axis=1 -> int64", nb + 64 * 4096 * 8, lambda: ms.argmax(x, axis=1, out=am))
+    del am
+    cs = ms.cumsum(x, axis=-1)
+    emit("C3", "cumsum axis=-1 (262144 rows of 4096)", 2 * nb, lambda: ms.cumsum(x, axis=-1, out=cs))
+    del cs
+    cf = ms.cumsum(x)
+    emit("C3", "cumsum axis=None (2^30, one decoupled look-back scan)", 2 * nb, lambda: ms.cumsum(x, out=cf))
+    del cf, x, xt
+
+    # C4: 2^30 casts / f16 pow / compares, complex64 mul of 2^27
+    gen.manual_seed(4)
+    n = 1 << 30
+    x, xt = dev((n,), "f32")
+    xt.normal_(generator=gen)
+    xb = x.astype("bf16")
+    back = xb.astype("f32")
+    emit("C4", "astype f32->bf16 2^30", n * 6, lambda: ms.astype(x, "bf16", out=xb))
+    emit("C4", "astype bf16->f32 2^30", n * 6, lambda: ms.astype(xb, "f32", out=back))
+    del x, xt, xb, back
+    a, at = dev((n,), "f16")
+    at.uniform_(0.1, 4.0, generator=gen)
+    b, bt = dev((n,), "f16")
+    bt.uniform_(-2.0, 2.0, generator=gen)
+    p = ms.pow(a, b)
+    emit("C4", "pow f16 2^30", n * 6, lambda: ms.pow(a, b, out=p))
+    del p
+    lt = ms.lt(a, b)
+    emit("C4", "lt f16 -> bool 2^30", n * 5, lambda: ms.lt(a, b, out=lt))
+    emit("C4", "eq f16 -> bool 2^30", n * 5, lambda: ms.eq(a, b, out=lt))
+    del a, at, b, bt, lt
+    m = 1 << 27
+    z1, z1t = dev((m,), "c64")
+    torch.view_as_real(z1t).normal_(generator=gen)
+    z2, z2t = dev((m,), "c64")
+    torch.view_as_real(z2t).normal_(generator=gen)
+    z = ms.mul(z1, z2)
+    emit("C4", "mul c64 2^27", m * 24, lambda: ms.mul(z1, z2, out=z))
+    del z1, z1t, z2, z2t, z
+
+    # the transposed copies of the views row (contiguous() of a transpose)
+    q = 16384
+    for dt_, esz in (("f32", 4), ("f16", 2)):
+        v, vt = dev((q, q), dt_)
+        vt.normal_(generator=gen)
+        t = ms.contiguous(ms.transpose(v))
+        emit("views", f"contiguous(transpose) {dt_} (16384,16384)", 2 * q * q * esz,
+             lambda v=v, t=t: ms.contiguous(ms.transpose(v), out=t))
+        del v, vt, t
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    del np
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -659,6 +952,7 @@ def main() -> None:
     ap.add_argument("--sample-rows", type=int, default=2048, help="rows of the CPU sample")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-suite", action="store_true", help="skip the per-op table of the other workloads")
     ap.add_argument("--suite", default="", help="comma list of C1..C4, NEXT: time every op of those configs")
     ap.add_argument("--scale", type=int, default=1,
                     help="with --suite: divide the large extents of C2-C4 by this power of two (profiling runs)")

@@ -184,15 +184,20 @@ def broadcast_shape(*shapes):
     return np.broadcast_shapes(*shapes)
 
 
-def binary(op: str, a: np.ndarray, b: np.ndarray, compute: int | None = None, all_gpu: bool = False) -> np.ndarray:
+def binary(op: str, a: np.ndarray, b: np.ndarray, compute: int | None = None, all_gpu: bool = False,
+           out: np.ndarray | None = None) -> np.ndarray:
     """binary_elementwise on the CPU path: cast to the promoted dtype, then
-    c[i] = op(a[off_a], b[off_b]) in that dtype."""
+    c[i] = op(a[off_a], b[off_b]) in that dtype (into `out` when given: a
+    C-contiguous array of the result's shape and dtype)."""
     a, b = np.asarray(a), np.asarray(b)
     cd = compute if compute is not None else promote(code_of(a.dtype), code_of(b.dtype), all_gpu)
     a2, b2 = _as(a, cd), _as(b, cd)
     shape = broadcast_shape(a2.shape, b2.shape)
     av, bv = np.broadcast_to(a2, shape), np.broadcast_to(b2, shape)
-    out = np.empty(shape, dtype=_NP[cd])
+    if out is None:
+        out = np.empty(shape, dtype=_NP[cd])
+    elif out.shape != tuple(shape) or out.dtype != _NP[cd] or not out.flags.c_contiguous:
+        raise ValueError("binary: out must be C-contiguous with the result's shape and dtype")
     if out.size:
         lib().or_binary(OPS[op], cd, _ptr(av), _ptr(bv), _ptr(out), len(shape), _i64(shape),
                         _i64(_estrides(av)), _i64(_estrides(bv)))
