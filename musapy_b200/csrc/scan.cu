@@ -72,35 +72,39 @@ MPB_D void row_offsets(const ScanDev& g, int64_t o, int64_t& oi, int64_t& oo) {
   }
 }
 
-// Scan one tile of up to kTile elements starting at element `t0` of a row.
-// Returns the tile total (block-uniform). `carry` is added to every output.
+// One tile of up to kTile elements of a row, scanned in two phases so that
+// its values stay in registers in between: tile_scan loads the tile and scans
+// it (each thread's vectors sequentially, lanes by a warp shuffle scan, warps
+// through shared memory) and returns the tile total (block-uniform);
+// tile_store adds `carry` and the warp's prefix and writes the tile.
 template <class In, class Acc>
 struct Tile {
   static constexpr int VEC = 16 / sizeof(Acc);
   static constexpr int kWarpElems = kScanJ * 32 * VEC;
   static constexpr int kTile = (kScanThreads / 32) * kWarpElems;
+  Acc v[kScanJ][VEC];
+  Acc wpre;  // sum of the warps before this one
+  bool full;
 };
 
 template <class In, class Acc>
-MPB_D Acc scan_tile(const In* __restrict__ in, Acc* __restrict__ out, int64_t n, bool vec_ok, Acc carry,
-                    Acc* s_warp /* [8] */, bool publish_only_total, Acc* total_out) {
+MPB_D Acc tile_scan(Tile<In, Acc>& T, const In* __restrict__ in, int64_t n, bool vec_ok, Acc* s_warp /* [8] */) {
   using TL = Tile<In, Acc>;
   constexpr int VEC = TL::VEC;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  Acc v[kScanJ][VEC];
   const int64_t wbase = (int64_t)warp * TL::kWarpElems;
-  const bool full = vec_ok && (n >= TL::kTile);
+  T.full = vec_ok && (n >= TL::kTile);
 #pragma unroll
   for (int j = 0; j < kScanJ; ++j) {
     const int64_t e = wbase + (int64_t)j * 32 * VEC + (int64_t)lane * VEC;
-    if (full) {
+    if (T.full) {
       const uint4 w = ld_stream16(in + e);
       const Acc* p = reinterpret_cast<const Acc*>(&w);
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[j][k] = p[k];
+      for (int k = 0; k < VEC; ++k) T.v[j][k] = p[k];
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[j][k] = (e + k < n) ? cvt<Acc>(in[e + k]) : Acc(0);
+      for (int k = 0; k < VEC; ++k) T.v[j][k] = (e + k < n) ? cvt<Acc>(in[e + k]) : Acc(0);
     }
   }
   // thread-sequential over each vector, warp scan over lanes, rows in order
@@ -108,14 +112,14 @@ MPB_D Acc scan_tile(const In* __restrict__ in, Acc* __restrict__ out, int64_t n,
 #pragma unroll
   for (int j = 0; j < kScanJ; ++j) {
 #pragma unroll
-    for (int k = 1; k < VEC; ++k) v[j][k] = sadd(v[j][k], v[j][k - 1]);
-    const Acc tot = v[j][VEC - 1];
+    for (int k = 1; k < VEC; ++k) T.v[j][k] = sadd(T.v[j][k], T.v[j][k - 1]);
+    const Acc tot = T.v[j][VEC - 1];
     const Acc incl = warp_incl_scan<Acc>(tot, lane);
     Acc excl = shfl_up<Acc>(incl, 1);
     if (lane == 0) excl = Acc(0);
     const Acc pre = sadd(run, excl);
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) v[j][k] = sadd(v[j][k], pre);
+    for (int k = 0; k < VEC; ++k) T.v[j][k] = sadd(T.v[j][k], pre);
     run = sadd(run, shfl_idx<Acc>(incl, 31));
   }
   // cross-warp scan of warp totals
@@ -128,25 +132,32 @@ MPB_D Acc scan_tile(const In* __restrict__ in, Acc* __restrict__ out, int64_t n,
     if (w < warp) wpre = sadd(wpre, t);
     total = sadd(total, t);
   }
-  if (total_out) *total_out = total;
-  if (publish_only_total) return total;
-  const Acc add = sadd(carry, wpre);
+  T.wpre = wpre;
+  return total;
+}
+
+template <class In, class Acc>
+MPB_D void tile_store(const Tile<In, Acc>& T, Acc* __restrict__ out, int64_t n, Acc carry) {
+  using TL = Tile<In, Acc>;
+  constexpr int VEC = TL::VEC;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t wbase = (int64_t)warp * TL::kWarpElems;
+  const Acc add = sadd(carry, T.wpre);
 #pragma unroll
   for (int j = 0; j < kScanJ; ++j) {
     const int64_t e = wbase + (int64_t)j * 32 * VEC + (int64_t)lane * VEC;
-    if (full) {
+    if (T.full) {
       uint4 w;
       Acc* p = reinterpret_cast<Acc*>(&w);
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) p[k] = sadd(v[j][k], add);
+      for (int k = 0; k < VEC; ++k) p[k] = sadd(T.v[j][k], add);
       st_stream16(out + e, w);
     } else {
 #pragma unroll
       for (int k = 0; k < VEC; ++k)
-        if (e + k < n) out[e + k] = sadd(v[j][k], add);
+        if (e + k < n) out[e + k] = sadd(T.v[j][k], add);
     }
   }
-  return total;
 }
 
 // ----------------------------------------------------------------- ROWS
@@ -160,8 +171,9 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_rows(const In* __restrict
     row_offsets(g, o, oi, oo);
     Acc carry = Acc(0);
     for (int64_t t0 = 0; t0 < g.L; t0 += TL::kTile) {
-      Acc total;
-      scan_tile<In, Acc>(a + oi + t0, out + oo + t0, g.L - t0, vec_ok != 0, carry, s_warp, false, &total);
+      TL T;
+      const Acc total = tile_scan<In, Acc>(T, a + oi + t0, g.L - t0, vec_ok != 0, s_warp);
+      tile_store<In, Acc>(T, out + oo + t0, g.L - t0, carry);
       carry = sadd(carry, total);
     }
   }
@@ -216,11 +228,10 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __rest
   const In* in = a + oi + t0;
   Acc* dst = out + oo + t0;
   const int64_t n = g.L - t0;
-  // pass 1: tile total only (values stay in registers of scan_tile's caller
-  // is not possible across the wait, so the tile is scanned once the prefix
-  // is known; the total comes from the same loads)
-  Acc total;
-  scan_tile<In, Acc>(in, dst, n, vec_ok != 0, Acc(0), s_warp, true, &total);
+  // the tile is read once: scanned into registers, its total published, the
+  // prefix found by looking back, then the registers written out
+  TL T;
+  const Acc total = tile_scan<In, Acc>(T, in, n, vec_ok != 0, s_warp);
   if (threadIdx.x == 0) {
     volatile int* vf = flags;
     if (t == 0) {
@@ -250,8 +261,7 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __rest
     }
   }
   __syncthreads();
-  const Acc carry = s_prefix;
-  scan_tile<In, Acc>(in, dst, n, vec_ok != 0, carry, s_warp, false, nullptr);
+  tile_store<In, Acc>(T, dst, n, s_prefix);
 }
 
 // ----------------------------------------------------------------- COLS

@@ -404,20 +404,27 @@ def _reduce(kernel: str, a: Array, axis, keepdims: bool, out):
             f"{kernel}: ordering reduction not supported for complex dtype {a.dtype} (complex has no total order)"
         )
     axes = _resolve_axes(axis, a.ndim)
-    if len(axes) > 1 and out is not None:
-        raise errors.ShapeError("reduction with multiple axes does not support out= yet")
     if (kernel in ("max", "min") and axis is not None and len(axes) > 1
             and a.dtype.code in (_dt.F16, _dt.BF16, _dt.F32, _dt.F64)):
         # reduce_multi (reduction.rs:118-223) reduces one axis at a time, in
         # ascending order. For float max/min that order is visible: a NaN at
         # the start of an inner run, or the sign of a zero extremum, decides
-        # the outcome per pass, so the passes are kept.
+        # the outcome per pass, so the passes are kept. The last pass writes
+        # into `out` (through a keepdims-shaped view of it) when one is given.
+        kshape = tuple(1 if i in axes else s for i, s in enumerate(a.shape))
+        rshape = kshape if keepdims else tuple(s for i, s in enumerate(a.shape) if i not in axes)
+        if out is not None:
+            _check_out(out, rshape, a.dtype, a._dev, kernel)
+            if _alias(out, a):
+                raise errors.MemoryError("out= aliases an input buffer (AliasDetected)")
         cur = a
-        for ax in sorted(axes):
+        axs = sorted(axes)
+        for ax in axs[:-1]:
             cur = _reduce(kernel, cur, ax, True, None)
-        if keepdims:
-            return cur
-        return reshape(cur, tuple(s for i, s in enumerate(a.shape) if i not in axes))
+        cur = _reduce(kernel, cur, axs[-1], True, reshape(out, kshape) if out is not None else None)
+        if out is not None:
+            return out
+        return cur if keepdims else reshape(cur, rshape)
     red = axes if axes else list(range(a.ndim))
     is_arg = kernel in ("argmax", "argmin")
     cd = _compute_dtype(a.dtype, kernel)

@@ -330,6 +330,34 @@ def test_reduce_prod_and_keepdims(ms, oracle):
             assert got.shape == want.shape, (op, axis)
 
 
+@pytest.mark.parametrize("keepdims", [False, True])
+def test_reduce_multi_axis_into_out(ms, oracle, keepdims):
+    """Reductions over several axes written into a caller's out= array: the
+    one-pass kernels (sum, mean, argmax over merged axes) and the per-axis
+    passes of float max/min (the last pass writes into out), with a NaN at
+    the start of an inner run and signed zeros so the pass order shows."""
+    rng = np.random.default_rng(16)
+    x = rng.standard_normal((6, 40, 33)).astype(np.float32)
+    x[2, 0, 0] = np.nan
+    x[4, :, 5] = 0.0
+    x[4, 3, 5] = -0.0
+    xd = dev(ms, x)
+    for op in ["sum", "mean", "max", "min", "argmax", "argmin"]:
+        for axis in [(0, 2), (1, 2), (0, 1, 2)]:
+            want = oracle.reduce(op, x, axis, keepdims=keepdims)
+            dt = "i64" if op.startswith("arg") else "f32"
+            out = ms.empty(want.shape, dt)
+            got = getattr(ms, op)(xd, axis=axis, keepdims=keepdims, out=out)
+            assert got is out
+            if op in ("sum", "mean"):
+                assert_sum_close(out.numpy(), want, oracle.reduce("sum", np.abs(x).astype(np.float64), axis,
+                                                                  keepdims=keepdims), 1e-5, f"{op} {axis}")
+            else:
+                assert_bits_equal(out.numpy(), want, f"{op} {axis} keepdims={keepdims}")
+    with pytest.raises(ms.ShapeError):
+        ms.max(xd, axis=(0, 2), out=ms.empty((41,), "f32"))
+
+
 def test_reduce_nan_ties_signed_zero(ms, oracle):
     """First occurrence on ties, NaN only when it is the first element,
     +0/-0 resolved by position - bit-identical to the sequential CPU loop."""
