@@ -725,6 +725,16 @@ def run_suite(args) -> None:
         emit("C4", "mul c64 2^27", d["z1"].size * 24, lambda: ms.mul(z1, z2, out=z),
              cpu=(lambda: O.binary("mul", z1s, z2s), m * 24, "first 2^22 elements"))
         del z1, z2, z, d
+    if "VIEWS" in cfgs:
+        # contiguous() of transposed 16384^2 views (the padded-tile kernel for
+        # 4-byte elements, TMA tiles for 2-byte ones); small enough to profile
+        q = 16384
+        for dt_, esz in (("f32", 4), ("f16", 2)):
+            v = ms.reshape(ms.arange(q * q, dtype=dt_), (q, q))
+            t = ms.contiguous(ms.transpose(v))
+            emit("VIEWS", f"contiguous(transpose) {dt_} (16384,16384)", 2 * q * q * esz,
+                 lambda v=v, t=t: ms.contiguous(ms.transpose(v), out=t))
+            del v, t
     if "NEXT" in cfgs:
         # the rows around the hot path: contiguous copies of views, creation
         # kernels, host <-> device transfers (device-side bytes = read + write)
@@ -953,7 +963,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-suite", action="store_true", help="skip the per-op table of the other workloads")
-    ap.add_argument("--suite", default="", help="comma list of C1..C4, NEXT: time every op of those configs")
+    ap.add_argument("--suite", default="", help="comma list of C1..C4, VIEWS, NEXT: time every op of those configs")
     ap.add_argument("--scale", type=int, default=1,
                     help="with --suite: divide the large extents of C2-C4 by this power of two (profiling runs)")
     ap.add_argument("--suite-cpu", action="store_true",
