@@ -20,6 +20,7 @@
 //             the same order as the CPU loop (op_builder.rs:3640-3688);
 //   GEN       anything else: one thread per row, sequential.
 #include <stdint.h>
+#include <string.h>
 #include "common.cuh"
 #include "internal.h"
 #include "plan.h"
@@ -38,6 +39,10 @@ template <class T> MPB_D T shfl_up(T x, int o);
 template <> MPB_D float shfl_up<float>(float x, int o) { return __shfl_up_sync(0xffffffffu, x, o); }
 template <> MPB_D double shfl_up<double>(double x, int o) { return __shfl_up_sync(0xffffffffu, x, o); }
 template <> MPB_D int64_t shfl_up<int64_t>(int64_t x, int o) { return __shfl_up_sync(0xffffffffu, (long long)x, o); }
+template <class T> MPB_D T shfl_x(T x, int o);
+template <> MPB_D float shfl_x<float>(float x, int o) { return __shfl_xor_sync(0xffffffffu, x, o); }
+template <> MPB_D double shfl_x<double>(double x, int o) { return __shfl_xor_sync(0xffffffffu, x, o); }
+template <> MPB_D int64_t shfl_x<int64_t>(int64_t x, int o) { return __shfl_xor_sync(0xffffffffu, (long long)x, o); }
 template <class T> MPB_D T shfl_idx(T x, int l);
 template <> MPB_D float shfl_idx<float>(float x, int l) { return __shfl_sync(0xffffffffu, x, l); }
 template <> MPB_D double shfl_idx<double>(double x, int l) { return __shfl_sync(0xffffffffu, x, l); }
@@ -180,26 +185,98 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_rows(const In* __restrict
 }
 
 // ------------------------------------------------------------- LOOKBACK
-// Scratch layout: [u32 ticket][i32 status][pad 8] then per tile:
-// flags (i32, 0 = none, 1 = aggregate ready, 2 = inclusive prefix ready),
-// then aggregates (Acc), then inclusive prefixes (Acc).
-constexpr int64_t kSpinLimit = 1 << 22;  // polls per predecessor before giving up
+// Scratch layout: [u32 ticket][i32 status][pad 8] then one 16-byte
+// descriptor per tile: two 8-byte words {flag << 32 | value bits low half,
+// flag << 32 | value bits high half}, flag 1 = the tile's aggregate, 2 = its
+// inclusive prefix (0 = nothing yet; the scratch is zeroed per call). Each
+// word is written and read as one naturally aligned 8-byte access, so a
+// reader that sees the same flag in both words holds the value written with
+// it: no fence is needed between a value and its flag.
+//
+// Look-back (Merrill & Garland 2016, with a wide window): warp 0 reads the
+// descriptors of the kLookWindow tiles before this one in one round of loads
+// (kLookPerLane consecutive descriptors per lane), waits (bounded) until each
+// has a flag, finds the nearest inclusive prefix and adds it to the
+// aggregates in between; with none in the window it adds all of them and
+// moves the window back. Tiles take their index from an atomic ticket, so
+// every predecessor has started. The window is wide enough that the nearest
+// inclusive prefix lies inside it in the steady state: about (tiles started
+// per second) x (half an L2 round trip) tiles back.
+constexpr int64_t kSpinLimit = 1 << 22;  // polls per descriptor before giving up
+constexpr int kLookPerLane = 4;
+constexpr int kLookWindow = 32 * kLookPerLane;
 
 template <class Acc>
-MPB_D int wait_flag(volatile int* f, int* status) {
-  int v = *f;
+MPB_D void desc_publish(unsigned long long* d, Acc v, unsigned flag) {
+  static_assert(sizeof(Acc) == 4 || sizeof(Acc) == 8, "4- or 8-byte accumulators");
+  unsigned long long bits = 0;
+  memcpy(&bits, &v, sizeof(Acc));
+  const unsigned long long f = (unsigned long long)flag << 32;
+  const unsigned long long w0 = f | (bits & 0xffffffffull), w1 = f | (bits >> 32);
+  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(d), "l"(w0), "l"(w1) : "memory");
+}
+
+// Reads descriptor `d` until it holds a flag (both words agree); returns the
+// flag (0 when the bounded wait gave up, recorded in `status`).
+template <class Acc>
+MPB_D unsigned desc_wait(const unsigned long long* d, Acc& v, int* status) {
+  unsigned long long w0, w1;
   int64_t spins = 0;
   unsigned ns = 32;
-  while (v == 0) {
+  for (;;) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(d) : "memory");
+    const unsigned f0 = (unsigned)(w0 >> 32), f1 = (unsigned)(w1 >> 32);
+    if (f0 != 0 && f0 == f1) {
+      const unsigned long long bits = (w0 & 0xffffffffull) | ((w1 & 0xffffffffull) << 32);
+      memcpy(&v, &bits, sizeof(Acc));
+      return f0;
+    }
     if (++spins > kSpinLimit) {
       atomicOr(status, 1 << MPB_ERR_TIMEOUT);
+      v = Acc(0);
       return 0;
     }
     __nanosleep(ns);
     if (ns < 256) ns <<= 1;
-    v = *f;
   }
-  return v;
+}
+
+// Exclusive prefix of tile `tid` (local index `t` in its row), run by warp 0.
+template <class Acc>
+MPB_D Acc look_back(const unsigned long long* desc, int64_t tid, int64_t t, int* status) {
+  const int lane = threadIdx.x & 31;
+  Acc excl = Acc(0);
+  int64_t back = 0;  // tiles already covered behind this one
+  for (;;) {
+    Acc v[kLookPerLane];
+    unsigned f[kLookPerLane];
+    // distance of slot k of this lane: back + lane * kLookPerLane + k + 1
+#pragma unroll
+    for (int k = 0; k < kLookPerLane; ++k) {
+      const int64_t dist = back + (int64_t)lane * kLookPerLane + k + 1;
+      f[k] = 3;  // beyond the row start: no tile (never reached, see below)
+      v[k] = Acc(0);
+      if (dist <= t) f[k] = desc_wait<Acc>(desc + 2 * (tid - dist), v[k], status);
+    }
+    // nearest inclusive prefix (flag 2) in the window, or a given-up wait
+    // (flag 0: stop there and report through the status word)
+    int kn = kLookPerLane;
+#pragma unroll
+    for (int k = kLookPerLane - 1; k >= 0; --k)
+      if (f[k] == 2 || f[k] == 0) kn = k;
+    const int my_stop = kn < kLookPerLane ? lane * kLookPerLane + kn : 0x7fffffff;
+    const int stop = __reduce_min_sync(0xffffffffu, my_stop);
+    Acc part = Acc(0);
+#pragma unroll
+    for (int k = 0; k < kLookPerLane; ++k)
+      if (lane * kLookPerLane + k <= stop && f[k] != 3) part = sadd(part, v[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part = sadd(part, shfl_x<Acc>(part, o));
+    excl = sadd(excl, part);
+    if (stop != 0x7fffffff) return excl;
+    back += kLookWindow;
+    if (back >= t) return excl;  // the whole row was aggregates: cannot happen (tile 0 is inclusive)
+  }
 }
 
 template <class In, class Acc>
@@ -212,10 +289,8 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __rest
   __shared__ Acc s_prefix;
   unsigned* ticket = reinterpret_cast<unsigned*>(scratch);
   int* status = reinterpret_cast<int*>(scratch + 4);
+  unsigned long long* desc = reinterpret_cast<unsigned long long*>(scratch + 16);
   const int64_t ntiles = g.M * tiles_per_row;
-  int* flags = reinterpret_cast<int*>(scratch + 16);
-  Acc* aggs = reinterpret_cast<Acc*>(scratch + 16 + ((ntiles * 4 + 15) / 16) * 16);
-  Acc* incs = aggs + ntiles;
   if (threadIdx.x == 0) s_ticket = atomicAdd(ticket, 1u);
   __syncthreads();
   const int64_t tid = s_ticket;
@@ -228,36 +303,23 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __rest
   const In* in = a + oi + t0;
   Acc* dst = out + oo + t0;
   const int64_t n = g.L - t0;
-  // the tile is read once: scanned into registers, its total published, the
-  // prefix found by looking back, then the registers written out
+  // the tile is read once: scanned into registers, its aggregate published,
+  // its prefix found by looking back, then the registers written out
   TL T;
   const Acc total = tile_scan<In, Acc>(T, in, n, vec_ok != 0, s_warp);
-  if (threadIdx.x == 0) {
-    volatile int* vf = flags;
+  if (threadIdx.x < 32) {
     if (t == 0) {
-      incs[tid] = total;
-      __threadfence();
-      vf[tid] = 2;
-      s_prefix = Acc(0);
-    } else {
-      aggs[tid] = total;
-      __threadfence();
-      vf[tid] = 1;
-      Acc excl = Acc(0);
-      for (int64_t p = tid - 1; p >= tid - t; --p) {
-        const int f = wait_flag<Acc>(vf + p, status);
-        __threadfence();
-        if (f == 2) {
-          excl = sadd(excl, *(volatile Acc*)(incs + p));
-          break;
-        }
-        if (f == 0) break;  // the wait gave up (recorded in the status word): stop looking back
-        excl = sadd(excl, *(volatile Acc*)(aggs + p));
+      if (threadIdx.x == 0) {
+        desc_publish<Acc>(desc + 2 * tid, total, 2u);
+        s_prefix = Acc(0);
       }
-      incs[tid] = sadd(excl, total);
-      __threadfence();
-      vf[tid] = 2;
-      s_prefix = excl;
+    } else {
+      if (threadIdx.x == 0) desc_publish<Acc>(desc + 2 * tid, total, 1u);
+      const Acc excl = look_back<Acc>(desc, tid, t, status);
+      if (threadIdx.x == 0) {
+        desc_publish<Acc>(desc + 2 * tid, sadd(excl, total), 2u);
+        s_prefix = excl;
+      }
     }
   }
   __syncthreads();
@@ -357,7 +419,7 @@ ScanPlan scan_plan(const ScanReq& r) {
 
 template <class Acc>
 size_t lookback_bytes(int64_t ntiles) {
-  return 16 + (size_t)((ntiles * 4 + 15) / 16) * 16 + (size_t)ntiles * 2 * sizeof(Acc);
+  return 16 + (size_t)ntiles * 16;
 }
 
 template <class In, class Acc>

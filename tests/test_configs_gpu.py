@@ -127,6 +127,28 @@ def test_config3_cumsum_last_axis_every_element(ms, oracle, c3, compared):
     compared("cumsum within 1e-5*cumsum|x|", got.size)
 
 
+def test_config3_cumsum_flattened_every_element(ms, oracle, c3, compared):
+    """cumsum with axis=None over all 2^30 elements: one decoupled look-back
+    scan (262,144 tiles), against the oracle's sequential f32 running sum;
+    the f64 truth and the sum|x| scale are running sums in float64."""
+    x = c3.reshape(-1)
+    ms.ops.set_scan_status_check(True)
+    try:
+        got = ms.cumsum(ms.from_numpy(c3)).numpy()
+    finally:
+        ms.ops.set_scan_status_check(False)
+    want = oracle.cumsum(x, 0)
+    carry, carry_abs = 0.0, 0.0
+    step = 1 << 24
+    for i in range(0, x.size, step):
+        ch = x[i:i + step].astype(np.float64)
+        truth = np.cumsum(ch) + carry
+        absx = np.cumsum(np.abs(ch)) + carry_abs
+        assert_sum_close(got[i:i + step], want[i:i + step], absx, 1e-5, f"cumsum(axis=None) at {i}", truth=truth)
+        carry, carry_abs = truth[-1], absx[-1]
+    compared("cumsum(axis=None) within 1e-5*cumsum|x|", x.size)
+
+
 def test_config4_bf16_round_trip(ms, oracle, c4, compared):
     x = c4["x"]
     xd = ms.from_numpy(x)

@@ -468,7 +468,7 @@ def test_reduce_strided_views(ms, oracle):
 # ---------------------------------------------------------------- cumsum
 CUMSUM_CASES = [((4,), 0), ((2, 2), None), ((2, 2), 0), ((2, 2), 1), ((3, 70000), 1), ((1300,), 0), ((1537,), 0),
                 ((100_000,), 0), ((262, 4096), 1), ((64, 33, 5), 1), ((5000, 7), 0), ((1 << 21,), None),
-                ((400, 4097), -1)]
+                ((400, 4097), -1), (((1 << 24) + 5,), None), ((5, 3_000_001), 1)]
 
 
 @pytest.mark.parametrize("shape,axis", CUMSUM_CASES)
