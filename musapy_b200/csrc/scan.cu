@@ -82,25 +82,25 @@ MPB_D void row_offsets(const ScanDev& g, int64_t o, int64_t& oi, int64_t& oo) {
 // it (each thread's vectors sequentially, lanes by a warp shuffle scan, warps
 // through shared memory) and returns the tile total (block-uniform);
 // tile_store adds `carry` and the warp's prefix and writes the tile.
-template <class In, class Acc>
+template <class In, class Acc, int J = kScanJ>
 struct Tile {
   static constexpr int VEC = 16 / sizeof(Acc);
-  static constexpr int kWarpElems = kScanJ * 32 * VEC;
+  static constexpr int kWarpElems = J * 32 * VEC;
   static constexpr int kTile = (kScanThreads / 32) * kWarpElems;
-  Acc v[kScanJ][VEC];
+  Acc v[J][VEC];
   Acc wpre;  // sum of the warps before this one
   bool full;
 };
 
-template <class In, class Acc>
-MPB_D Acc tile_scan(Tile<In, Acc>& T, const In* __restrict__ in, int64_t n, bool vec_ok, Acc* s_warp /* [8] */) {
-  using TL = Tile<In, Acc>;
+template <class In, class Acc, int J>
+MPB_D Acc tile_scan(Tile<In, Acc, J>& T, const In* __restrict__ in, int64_t n, bool vec_ok, Acc* s_warp /* [8] */) {
+  using TL = Tile<In, Acc, J>;
   constexpr int VEC = TL::VEC;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t wbase = (int64_t)warp * TL::kWarpElems;
   T.full = vec_ok && (n >= TL::kTile);
 #pragma unroll
-  for (int j = 0; j < kScanJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int64_t e = wbase + (int64_t)j * 32 * VEC + (int64_t)lane * VEC;
     if (T.full) {
       const uint4 w = ld_stream16(in + e);
@@ -115,7 +115,7 @@ MPB_D Acc tile_scan(Tile<In, Acc>& T, const In* __restrict__ in, int64_t n, bool
   // thread-sequential over each vector, warp scan over lanes, rows in order
   Acc run = Acc(0);
 #pragma unroll
-  for (int j = 0; j < kScanJ; ++j) {
+  for (int j = 0; j < J; ++j) {
 #pragma unroll
     for (int k = 1; k < VEC; ++k) T.v[j][k] = sadd(T.v[j][k], T.v[j][k - 1]);
     const Acc tot = T.v[j][VEC - 1];
@@ -141,15 +141,15 @@ MPB_D Acc tile_scan(Tile<In, Acc>& T, const In* __restrict__ in, int64_t n, bool
   return total;
 }
 
-template <class In, class Acc>
-MPB_D void tile_store(const Tile<In, Acc>& T, Acc* __restrict__ out, int64_t n, Acc carry) {
-  using TL = Tile<In, Acc>;
+template <class In, class Acc, int J>
+MPB_D void tile_store(const Tile<In, Acc, J>& T, Acc* __restrict__ out, int64_t n, Acc carry) {
+  using TL = Tile<In, Acc, J>;
   constexpr int VEC = TL::VEC;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t wbase = (int64_t)warp * TL::kWarpElems;
   const Acc add = sadd(carry, T.wpre);
 #pragma unroll
-  for (int j = 0; j < kScanJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int64_t e = wbase + (int64_t)j * 32 * VEC + (int64_t)lane * VEC;
     if (T.full) {
       uint4 w;
@@ -177,8 +177,8 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_rows(const In* __restrict
     Acc carry = Acc(0);
     for (int64_t t0 = 0; t0 < g.L; t0 += TL::kTile) {
       TL T;
-      const Acc total = tile_scan<In, Acc>(T, a + oi + t0, g.L - t0, vec_ok != 0, s_warp);
-      tile_store<In, Acc>(T, out + oo + t0, g.L - t0, carry);
+      const Acc total = tile_scan(T, a + oi + t0, g.L - t0, vec_ok != 0, s_warp);
+      tile_store(T, out + oo + t0, g.L - t0, carry);
       carry = sadd(carry, total);
     }
   }
@@ -203,6 +203,14 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_rows(const In* __restrict
 // inclusive prefix lies inside it in the steady state: about (tiles started
 // per second) x (half an L2 round trip) tiles back.
 constexpr int64_t kSpinLimit = 1 << 22;  // polls per descriptor before giving up
+#ifndef MPB_SCAN_LB_J
+#define MPB_SCAN_LB_J 8
+#endif
+#ifndef MPB_SCAN_LB_MINB
+#define MPB_SCAN_LB_MINB 3
+#endif
+constexpr int kLookJ = MPB_SCAN_LB_J;        // vector rows per warp of a look-back tile
+constexpr int kLookMinBlocks = MPB_SCAN_LB_MINB;  // CTAs per SM the registers must allow
 constexpr int kLookPerLane = 4;
 constexpr int kLookWindow = 32 * kLookPerLane;
 
@@ -216,74 +224,82 @@ MPB_D void desc_publish(unsigned long long* d, Acc v, unsigned flag) {
   asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(d), "l"(w0), "l"(w1) : "memory");
 }
 
-// Reads descriptor `d` until it holds a flag (both words agree); returns the
-// flag (0 when the bounded wait gave up, recorded in `status`).
+// One read of descriptor `d`: its flag (0 = nothing yet, or the two words
+// disagree because a write landed between them) and value.
 template <class Acc>
-MPB_D unsigned desc_wait(const unsigned long long* d, Acc& v, int* status) {
+MPB_D unsigned desc_read(const unsigned long long* d, Acc& v) {
   unsigned long long w0, w1;
-  int64_t spins = 0;
-  unsigned ns = 32;
-  for (;;) {
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(d) : "memory");
-    const unsigned f0 = (unsigned)(w0 >> 32), f1 = (unsigned)(w1 >> 32);
-    if (f0 != 0 && f0 == f1) {
-      const unsigned long long bits = (w0 & 0xffffffffull) | ((w1 & 0xffffffffull) << 32);
-      memcpy(&v, &bits, sizeof(Acc));
-      return f0;
-    }
-    if (++spins > kSpinLimit) {
-      atomicOr(status, 1 << MPB_ERR_TIMEOUT);
-      v = Acc(0);
-      return 0;
-    }
-    __nanosleep(ns);
-    if (ns < 256) ns <<= 1;
-  }
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(d) : "memory");
+  const unsigned f0 = (unsigned)(w0 >> 32), f1 = (unsigned)(w1 >> 32);
+  const unsigned long long bits = (w0 & 0xffffffffull) | ((w1 & 0xffffffffull) << 32);
+  memcpy(&v, &bits, sizeof(Acc));
+  return f0 == f1 ? f0 : 0u;
 }
 
 // Exclusive prefix of tile `tid` (local index `t` in its row), run by warp 0.
+// Each round reads the whole window once; it is settled when the nearest
+// inclusive prefix in it (or the row start) has only aggregates in front of
+// it, and otherwise read again (bounded) - so a tile waits only for the
+// predecessors between itself and the nearest inclusive prefix, not for the
+// whole window.
 template <class Acc>
 MPB_D Acc look_back(const unsigned long long* desc, int64_t tid, int64_t t, int* status) {
   const int lane = threadIdx.x & 31;
   Acc excl = Acc(0);
   int64_t back = 0;  // tiles already covered behind this one
+  int64_t spins = 0;
+  unsigned ns = 32;
   for (;;) {
     Acc v[kLookPerLane];
     unsigned f[kLookPerLane];
-    // distance of slot k of this lane: back + lane * kLookPerLane + k + 1
+    // slot k of this lane: distance back + lane * kLookPerLane + k + 1
 #pragma unroll
     for (int k = 0; k < kLookPerLane; ++k) {
       const int64_t dist = back + (int64_t)lane * kLookPerLane + k + 1;
-      f[k] = 3;  // beyond the row start: no tile (never reached, see below)
+      f[k] = 3;  // before the row start: not a tile
       v[k] = Acc(0);
-      if (dist <= t) f[k] = desc_wait<Acc>(desc + 2 * (tid - dist), v[k], status);
+      if (dist <= t) f[k] = desc_read<Acc>(desc + 2 * (tid - dist), v[k]);
     }
-    // nearest inclusive prefix (flag 2) in the window, or a given-up wait
-    // (flag 0: stop there and report through the status word)
-    int kn = kLookPerLane;
+    // nearest inclusive prefix of the window (slot index), and nearest
+    // descriptor still without a flag
+    int my_inc = 0x7fffffff, my_zero = 0x7fffffff;
 #pragma unroll
-    for (int k = kLookPerLane - 1; k >= 0; --k)
-      if (f[k] == 2 || f[k] == 0) kn = k;
-    const int my_stop = kn < kLookPerLane ? lane * kLookPerLane + kn : 0x7fffffff;
-    const int stop = __reduce_min_sync(0xffffffffu, my_stop);
+    for (int k = kLookPerLane - 1; k >= 0; --k) {
+      if (f[k] == 2) my_inc = lane * kLookPerLane + k;
+      if (f[k] == 0) my_zero = lane * kLookPerLane + k;
+    }
+    const int inc = __reduce_min_sync(0xffffffffu, my_inc);
+    const int zero = __reduce_min_sync(0xffffffffu, my_zero);
+    if (zero < inc) {  // a predecessor in front of the nearest prefix has not published yet
+      if (++spins > kSpinLimit) {
+        // give up: report it and use what is there (the result is then wrong
+        // and the status word says so)
+        if (lane == 0) atomicOr(status, 1 << MPB_ERR_TIMEOUT);
+      } else {
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
+        continue;
+      }
+    }
     Acc part = Acc(0);
 #pragma unroll
     for (int k = 0; k < kLookPerLane; ++k)
-      if (lane * kLookPerLane + k <= stop && f[k] != 3) part = sadd(part, v[k]);
+      if (lane * kLookPerLane + k <= inc && f[k] != 3) part = sadd(part, v[k]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part = sadd(part, shfl_x<Acc>(part, o));
     excl = sadd(excl, part);
-    if (stop != 0x7fffffff) return excl;
+    if (inc != 0x7fffffff || spins > kSpinLimit) return excl;
     back += kLookWindow;
-    if (back >= t) return excl;  // the whole row was aggregates: cannot happen (tile 0 is inclusive)
+    if (back >= t) return excl;  // cannot happen: the row's tile 0 publishes an inclusive prefix
+    ns = 32;
   }
 }
 
 template <class In, class Acc>
-__global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __restrict__ a, Acc* __restrict__ out,
+__global__ void __launch_bounds__(kScanThreads, kLookMinBlocks) k_scan_lookback(const In* __restrict__ a, Acc* __restrict__ out,
                                                                  ScanDev g, int vec_ok, char* __restrict__ scratch,
                                                                  int64_t tiles_per_row) {
-  using TL = Tile<In, Acc>;
+  using TL = Tile<In, Acc, kLookJ>;
   __shared__ Acc s_warp[kScanThreads / 32];
   __shared__ uint32_t s_ticket;
   __shared__ Acc s_prefix;
@@ -306,7 +322,7 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __rest
   // the tile is read once: scanned into registers, its aggregate published,
   // its prefix found by looking back, then the registers written out
   TL T;
-  const Acc total = tile_scan<In, Acc>(T, in, n, vec_ok != 0, s_warp);
+  const Acc total = tile_scan(T, in, n, vec_ok != 0, s_warp);
   if (threadIdx.x < 32) {
     if (t == 0) {
       if (threadIdx.x == 0) {
@@ -323,7 +339,7 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_lookback(const In* __rest
     }
   }
   __syncthreads();
-  tile_store<In, Acc>(T, dst, n, s_prefix);
+  tile_store(T, dst, n, s_prefix);
 }
 
 // ----------------------------------------------------------------- COLS
@@ -403,13 +419,14 @@ ScanPlan scan_plan(const ScanReq& r) {
     g.kout[d] = ko[d];
   }
   const int sms = sm_count();
-  pl.tiles_per_row = cdiv(g.L, Tile<In, Acc>::kTile);
+  pl.tiles_per_row = cdiv(g.L, Tile<In, Acc>::kTile);  // rows kernel's tiles (kind decision)
   if ((g.sa == 1 || g.L == 1) && (g.so == 1 || g.L == 1)) {
     bool vec_ok = std::is_same<In, Acc>::value && (((uintptr_t)r.a & 15) == 0) && (((uintptr_t)r.out & 15) == 0);
     for (int d = 0; d < K && vec_ok; ++d)
       if ((ki[d] * (int64_t)sizeof(In)) % 16 || (ko[d] * (int64_t)sizeof(Acc)) % 16) vec_ok = false;
     pl.vec_ok = vec_ok;
     pl.kind = (g.M >= 2 * sms || pl.tiles_per_row <= 1) ? 0 : 1;
+    if (pl.kind == 1) pl.tiles_per_row = cdiv(g.L, Tile<In, Acc, kLookJ>::kTile);
   } else {
     pl.vec_ok = 0;
     pl.kind = 2;

@@ -36,7 +36,10 @@ constexpr int kTmaRows = 32;  // q rows per tile
 // Per box width (bytes of p per row): tiles in flight per warp and the
 // block's shared memory.
 constexpr int tma_stages(int boxb) { return boxb <= 128 ? 4 : 3; }
-constexpr int tma_smem_bytes(int boxb) { return kTmaWarps * tma_stages(boxb) * (kTmaRows * boxb + 8) + 128; }
+// bseg: bytes of the other operand's q segment carried in each stage (BMODE 3)
+constexpr int tma_smem_bytes(int boxb, int bseg = 0) {
+  return kTmaWarps * tma_stages(boxb) * (kTmaRows * boxb + bseg + 8) + 128;
+}
 
 struct TmaArgs {
   int64_t dp, dq;            // extents along p (unit stride in the input) and q (inner in the output)
@@ -105,6 +108,14 @@ MPB_D void tma_load_tile(uint32_t dst, const CUtensorMap* tm, int batched, int x
   }
 }
 
+// 1-D bulk copy global -> shared on the stage's mbarrier (both addresses
+// 16-byte aligned, size a multiple of 16; host-checked). No multicast.
+MPB_D void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 MPB_D uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -169,7 +180,10 @@ MPB_D void store_run(TO* dst, const TO (&v)[E]) {
 }
 
 // BMODE: 0 unary, 1 binary with the other operand constant along p (read
-// once per row run), 2 binary with any other strides.
+// once per row run), 2 binary with any other strides, 3 as 1 with that
+// operand contiguous along q: its 32-value segment of each tile arrives in
+// the stage with the tile, by a bulk copy on the same mbarrier (no global
+// load waits at the start of a tile).
 template <class Op, class TC, class TA, class TB, class TO, int NIN, int BMODE, int BOXB>
 __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_constant__ CUtensorMap tm, Op op,
                                                                   const TB* __restrict__ b, TO* __restrict__ out,
@@ -180,14 +194,19 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
   constexpr int RB = 32 / CH;                 // row blocks (of E rows) per pass
   constexpr int PASSES = kTmaRows / (RB * E);
   constexpr int STAGES = tma_stages(BOXB);
-  constexpr int TILE = kTmaRows * BOXB;
-  static_assert(CH <= 32 && PASSES >= 1, "tile shape does not fit the lane layout");
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
+  // other operand's segment per stage, padded so every stage (a TMA
+  // destination) stays 128-byte aligned
+  constexpr int BSEG = BMODE == 3 ? (kTmaRows * (int)sizeof(TBv) + 127) / 128 * 128 : 0;
+  constexpr int TILE = kTmaRows * BOXB;
+  constexpr int STAGE = TILE + BSEG;
+  static_assert(CH <= 32 && PASSES >= 1, "tile shape does not fit the lane layout");
+  static_assert(BSEG % 16 == 0, "segment must keep stages 16-byte aligned");
   extern __shared__ char tma_smem[];
   const uint32_t base = (smem_u32(tma_smem) + 127u) & ~127u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t stages = base + (uint32_t)(warp * STAGES * TILE);
-  const uint32_t bars = base + (uint32_t)(kTmaWarps * STAGES * TILE + warp * STAGES * 8);
+  const uint32_t stages = base + (uint32_t)(warp * STAGES * STAGE);
+  const uint32_t bars = base + (uint32_t)(kTmaWarps * STAGES * STAGE + warp * STAGES * 8);
   const int64_t gw = (int64_t)blockIdx.x * kTmaWarps + warp;
   const int64_t nw = (int64_t)gridDim.x * kTmaWarps;
   if (gw >= t.ntiles) return;
@@ -195,9 +214,20 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
   auto issue = [&](int64_t ti, int s) {
     const TileIdx x = tma_tile(t, ti);
     const uint32_t bar = bars + 8u * (uint32_t)s;
-    mbar_expect_tx(bar, TILE);
-    tma_load_tile(stages + (uint32_t)(s * TILE), &tm, t.batched, (int)(x.tp * PX), (int)(x.tq * kTmaRows),
-                  (int)x.bi, bar);
+    const uint32_t dst = stages + (uint32_t)(s * STAGE);
+    uint32_t bbytes = 0;
+    if constexpr (BMODE == 3) {
+      // the segment's values along q (fewer on the last tile row; the
+      // host checked that every segment is a whole number of 16 bytes)
+      const int64_t q0 = x.tq * kTmaRows;
+      const int64_t nq = t.dq - q0 < kTmaRows ? t.dq - q0 : kTmaRows;
+      bbytes = nq > 0 ? (uint32_t)(nq * (int64_t)sizeof(TBv)) : 0u;
+    }
+    mbar_expect_tx(bar, TILE + bbytes);
+    tma_load_tile(dst, &tm, t.batched, (int)(x.tp * PX), (int)(x.tq * kTmaRows), (int)x.bi, bar);
+    if constexpr (BMODE == 3) {
+      if (bbytes) bulk_load(dst + TILE, reinterpret_cast<const TBv*>(b) + x.tq * kTmaRows, bbytes, bar);
+    }
   };
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(bars + 8u * (uint32_t)s, 1);
@@ -221,12 +251,22 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
       return;
     }
     const TileIdx x = tma_tile(t, ti);
-    const uint32_t tile = stages + (uint32_t)(s * TILE);
+    const uint32_t tile = stages + (uint32_t)(s * STAGE);
     const int64_t p0 = x.tp * PX + c * E, q0 = x.tq * kTmaRows;
     TO* ob = out + x.bi * t.bso;
     // the other operand along q for every pass, loaded up front so that
     // their latencies overlap (one wait per tile, not one per pass)
-    TC bq_all[NIN == 2 && BMODE == 1 ? PASSES : 1][E];
+    TC bq_all[NIN == 2 && (BMODE == 1 || BMODE == 3) ? PASSES : 1][E];
+    if constexpr (NIN == 2 && BMODE == 3) {
+      const char* seg = tma_smem + (tile + TILE - smem_u32(tma_smem));
+#pragma unroll
+      for (int pass = 0; pass < PASSES; ++pass) {
+        const int r0 = (pass * RB + qb) * E;
+#pragma unroll
+        for (int k2 = 0; k2 < E; ++k2)
+          bq_all[pass][k2] = q0 + r0 < t.dq ? cvt<TC>(reinterpret_cast<const TBv*>(seg)[r0 + k2]) : TC{};
+      }
+    }
     if constexpr (NIN == 2 && BMODE == 1) {
       const TBv* bb = reinterpret_cast<const TBv*>(b) + x.bi * t.bsb;
 #pragma unroll
@@ -257,7 +297,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
             const TC av = cvt<TC>(reinterpret_cast<const TA*>(&v[k2])[j]);
             if constexpr (NIN == 2) {
               TC bv;
-              if constexpr (BMODE == 1) {
+              if constexpr (BMODE == 1 || BMODE == 3) {
                 bv = bq_all[pass][k2];
               } else {
                 bv = cvt<TC>(reinterpret_cast<const TBv*>(b)[x.bi * t.bsb + p * t.sb_p + (q + k2) * t.sb_q]);
@@ -295,7 +335,6 @@ template <class Op, class TC, class TA, class TB, class TO, int NIN, int BOXB, i
 int launch_tiled_tma(const Op& op, const TA* a, const TB* b, TO* out, const TiledArgs& ta, int* err, cudaStream_t s) {
   constexpr int SZ = (int)sizeof(TA);
   constexpr int PX = BOXB / SZ;
-  constexpr int SMEM = tma_smem_bytes(BOXB);
   CUtensorMap tm;
   const int64_t nbatch = ta.nb ? ta.bshape[0] : 1;
   if (tma_encode(&tm, a, SZ, ta.dp, ta.dq, nbatch, ta.sa_q * SZ, ta.nb ? ta.bsa[0] * SZ : 0, PX, kTmaRows) != 0)
@@ -318,7 +357,7 @@ int launch_tiled_tma(const Op& op, const TA* a, const TB* b, TO* out, const Tile
   t.bsb = ta.nb ? ta.bsb[0] : 0;
   t.batched = nbatch > 1 ? 1 : 0;  // the same rule as tma_encode's rank
   t.err = err;
-  auto launch = [&](auto kernel) -> int {
+  auto launch = [&](auto kernel, int SMEM) -> int {
     // per call: the attribute belongs to the current device
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess) {
       (void)cudaGetLastError();
@@ -333,10 +372,17 @@ int launch_tiled_tma(const Op& op, const TA* a, const TB* b, TO* out, const Tile
     return launch_check("ew_tiled_tma");
   };
   if constexpr (NIN == 1) {
-    return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 1, 0, BOXB>);
+    return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 1, 0, BOXB>, tma_smem_bytes(BOXB));
   } else {
-    if (ta.sb_p == 0) return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 1, BOXB>);
-    return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 2, BOXB>);
+    constexpr int BSEG = (kTmaRows * (int)sizeof(TB) + 127) / 128 * 128;
+    // the other operand contiguous along q, 16-byte aligned, every tile's
+    // segment (32 values, fewer on the last tile row) a whole number of
+    // 16-byte units: it rides in the stages
+    if (ta.sb_p == 0 && ta.sb_q == 1 && !t.batched && (kTmaRows * (int)sizeof(TB)) % 16 == 0 &&
+        ((uintptr_t)b & 15) == 0 && (ta.dq * (int64_t)sizeof(TB)) % 16 == 0)
+      return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 3, BOXB>, tma_smem_bytes(BOXB, BSEG));
+    if (ta.sb_p == 0) return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 1, BOXB>, tma_smem_bytes(BOXB));
+    return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 2, BOXB>, tma_smem_bytes(BOXB));
   }
 }
 
