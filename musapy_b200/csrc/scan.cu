@@ -21,6 +21,7 @@
 //   GEN       anything else: one thread per row, sequential.
 #include <stdint.h>
 #include <string.h>
+#include "async_copy.cuh"
 #include "common.cuh"
 #include "internal.h"
 #include "plan.h"
@@ -342,6 +343,137 @@ __global__ void __launch_bounds__(kScanThreads, kLookMinBlocks) k_scan_lookback(
   tile_store(T, dst, n, s_prefix);
 }
 
+// LOOKBACK with the tile in shared memory (contiguous rows of a float or
+// int64 type, 16-byte aligned): one bulk copy brings a 32 KiB tile in,
+// the scan runs in place row by row, the aggregate is published, warp 0
+// looks back, and the threads add the prefix on the way out. The tile's
+// values wait out the look-back in shared memory instead of registers, so
+// a thread needs few registers and six CTAs fit on an SM: twice the tiles
+// in flight of the register tile, which is what a look-back scan's
+// bandwidth depends on (each tile waits for the predecessors between it and
+// the nearest published prefix).
+constexpr int kSmemTileBytes = 32768;
+#ifndef MPB_SCAN_SMEM_MINB
+#define MPB_SCAN_SMEM_MINB 6
+#endif
+
+template <class Acc>
+struct SmemTile {
+  static constexpr int VEC = 16 / (int)sizeof(Acc);
+  static constexpr int kElems = kSmemTileBytes / (int)sizeof(Acc);
+  static constexpr int J = kElems / (kScanThreads * VEC);  // vector rows per warp
+  static constexpr int kWarpElems = J * 32 * VEC;
+};
+
+template <class Acc>
+__global__ void __launch_bounds__(kScanThreads, MPB_SCAN_SMEM_MINB)
+    k_scan_lookback_smem(const Acc* __restrict__ a, Acc* __restrict__ out, ScanDev g, char* __restrict__ scratch,
+                         int64_t tiles_per_row) {
+  using ST = SmemTile<Acc>;
+  constexpr int VEC = ST::VEC;
+  extern __shared__ __align__(128) char scan_smem[];
+  Acc* tile = reinterpret_cast<Acc*>(scan_smem);
+  __shared__ Acc s_warp[kScanThreads / 32];
+  __shared__ uint32_t s_ticket;
+  __shared__ Acc s_prefix;
+  __shared__ __align__(8) unsigned long long s_bar;
+  unsigned* ticket = reinterpret_cast<unsigned*>(scratch);
+  int* status = reinterpret_cast<int*>(scratch + 4);
+  unsigned long long* desc = reinterpret_cast<unsigned long long*>(scratch + 16);
+  const int64_t ntiles = g.M * tiles_per_row;
+  const uint32_t bar = smem_u32(&s_bar);
+  if (threadIdx.x == 0) {
+    s_ticket = atomicAdd(ticket, 1u);
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int64_t tid = s_ticket;
+  if (tid >= ntiles) return;
+  const int64_t row = tid / tiles_per_row;
+  const int64_t t = tid - row * tiles_per_row;
+  int64_t oi, oo;
+  row_offsets(g, row, oi, oo);
+  const int64_t t0 = t * ST::kElems;
+  const int64_t n = g.L - t0;
+  const int cnt = n < ST::kElems ? (int)n : ST::kElems;
+  const Acc* in = a + oi + t0;
+  Acc* dst = out + oo + t0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // load: one bulk copy of the tile's whole 16-byte units; the rest (a
+  // partial unit at the end of a row, then zeros) by the threads
+  const int bulk_elems = cnt / VEC * VEC;
+  if (threadIdx.x == 0 && bulk_elems > 0) {
+    mbar_expect_tx(bar, (uint32_t)(bulk_elems * sizeof(Acc)));
+    bulk_load(smem_u32(tile), in, (uint32_t)(bulk_elems * sizeof(Acc)), bar);
+  }
+  for (int e = bulk_elems + threadIdx.x; e < ST::kElems; e += kScanThreads) tile[e] = e < cnt ? in[e] : Acc(0);
+  if (bulk_elems > 0 && !mbar_wait(bar, 0)) {
+    if (threadIdx.x == 0) atomicOr(status, 1 << MPB_ERR_TIMEOUT);
+  }
+  __syncthreads();
+  // scan in place: thread-sequential over each vector, warp scan over lanes,
+  // rows in order (the register tile's arithmetic)
+  const int wbase = warp * ST::kWarpElems;
+  Acc run = Acc(0);
+#pragma unroll 2
+  for (int j = 0; j < ST::J; ++j) {
+    Acc* p = tile + wbase + j * 32 * VEC + lane * VEC;
+    uint4 w = *reinterpret_cast<const uint4*>(p);
+    Acc* v = reinterpret_cast<Acc*>(&w);
+#pragma unroll
+    for (int k = 1; k < VEC; ++k) v[k] = sadd(v[k], v[k - 1]);
+    const Acc incl = warp_incl_scan<Acc>(v[VEC - 1], lane);
+    Acc excl = shfl_up<Acc>(incl, 1);
+    if (lane == 0) excl = Acc(0);
+    const Acc pre = sadd(run, excl);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = sadd(v[k], pre);
+    *reinterpret_cast<uint4*>(p) = w;
+    run = sadd(run, shfl_idx<Acc>(incl, 31));
+  }
+  if (lane == 0) s_warp[warp] = run;
+  __syncthreads();
+  Acc wpre = Acc(0), total = Acc(0);
+  for (int w = 0; w < kScanThreads / 32; ++w) {
+    const Acc tw = s_warp[w];
+    if (w < warp) wpre = sadd(wpre, tw);
+    total = sadd(total, tw);
+  }
+  if (threadIdx.x < 32) {
+    if (t == 0) {
+      if (threadIdx.x == 0) {
+        desc_publish<Acc>(desc + 2 * tid, total, 2u);
+        s_prefix = Acc(0);
+      }
+    } else {
+      if (threadIdx.x == 0) desc_publish<Acc>(desc + 2 * tid, total, 1u);
+      const Acc excl = look_back<Acc>(desc, tid, t, status);
+      if (threadIdx.x == 0) {
+        desc_publish<Acc>(desc + 2 * tid, sadd(excl, total), 2u);
+        s_prefix = excl;
+      }
+    }
+  }
+  __syncthreads();
+  const Acc add = sadd(s_prefix, wpre);
+#pragma unroll 2
+  for (int j = 0; j < ST::J; ++j) {
+    const int e = wbase + j * 32 * VEC + lane * VEC;
+    uint4 w = *reinterpret_cast<const uint4*>(tile + e);
+    Acc* v = reinterpret_cast<Acc*>(&w);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = sadd(v[k], add);
+    if (e + VEC <= cnt) {
+      st_stream16(dst + e, w);
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k)
+        if (e + k < cnt) dst[e + k] = v[k];
+    }
+  }
+}
+
 // ----------------------------------------------------------------- COLS
 // One thread per column (innermost kept dim unit-stride in and out).
 template <class In, class Acc>
@@ -378,6 +510,7 @@ struct ScanPlan {
   ScanDev g;
   int kind;  // 0 rows, 1 lookback, 2 cols/gen (sequential per thread)
   int vec_ok;
+  int smem;  // look-back with shared-memory tiles
   int64_t tiles_per_row;
 };
 
@@ -426,9 +559,17 @@ ScanPlan scan_plan(const ScanReq& r) {
       if ((ki[d] * (int64_t)sizeof(In)) % 16 || (ko[d] * (int64_t)sizeof(Acc)) % 16) vec_ok = false;
     pl.vec_ok = vec_ok;
     pl.kind = (g.M >= 2 * sms || pl.tiles_per_row <= 1) ? 0 : 1;
-    if (pl.kind == 1) pl.tiles_per_row = cdiv(g.L, Tile<In, Acc, kLookJ>::kTile);
+    pl.smem = 0;
+#ifndef MPB_SCAN_NO_SMEM
+    // shared-memory tiles: input already in the accumulator type, every row
+    // start 16-byte aligned (the bulk copy's rule)
+    pl.smem = pl.kind == 1 && std::is_same<In, Acc>::value && vec_ok;
+#endif
+    if (pl.kind == 1)
+      pl.tiles_per_row = pl.smem ? cdiv(g.L, (int64_t)SmemTile<Acc>::kElems) : cdiv(g.L, Tile<In, Acc, kLookJ>::kTile);
   } else {
     pl.vec_ok = 0;
+    pl.smem = 0;
     pl.kind = 2;
   }
   return pl;
@@ -465,6 +606,16 @@ int scan_typed(const ScanReq& r, cudaStream_t s, size_t* need_only) {
       int rc = cuda_check(cudaMemsetAsync(r.scratch, 0, need, s), "cumsum scratch clear");
       if (rc) return rc;
       const int64_t ntiles = g.M * pl.tiles_per_row;
+      if constexpr (std::is_same<In, Acc>::value) {
+        if (pl.smem) {
+          if (cudaFuncSetAttribute(k_scan_lookback_smem<Acc>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSmemTileBytes) != cudaSuccess)
+            return cuda_check(cudaGetLastError(), "cumsum_lookback: shared memory size");
+          k_scan_lookback_smem<Acc><<<(unsigned)ntiles, kScanThreads, kSmemTileBytes, s>>>(
+              a, out, g, static_cast<char*>(r.scratch), pl.tiles_per_row);
+          return launch_check("cumsum_lookback_smem");
+        }
+      }
       k_scan_lookback<In, Acc><<<(unsigned)ntiles, kScanThreads, 0, s>>>(a, out, g, pl.vec_ok,
                                                                        static_cast<char*>(r.scratch),
                                                                        pl.tiles_per_row);
