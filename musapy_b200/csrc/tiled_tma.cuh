@@ -37,10 +37,7 @@ constexpr int kTmaRows = 32;  // q rows per tile
 // Per box width (bytes of p per row): tiles in flight per warp and the
 // block's shared memory.
 constexpr int tma_stages(int boxb) { return boxb <= 128 ? 4 : 3; }
-// bseg: bytes of the other operand's q segment carried in each stage (BMODE 3)
-constexpr int tma_smem_bytes(int boxb, int bseg = 0) {
-  return kTmaWarps * tma_stages(boxb) * (kTmaRows * boxb + bseg + 8) + 128;
-}
+constexpr int tma_smem_bytes(int boxb) { return kTmaWarps * tma_stages(boxb) * (kTmaRows * boxb + 8) + 128; }
 
 struct TmaArgs {
   int64_t dp, dq;            // extents along p (unit stride in the input) and q (inner in the output)
@@ -134,10 +131,9 @@ MPB_D void store_run(TO* dst, const TO (&v)[E]) {
 }
 
 // BMODE: 0 unary, 1 binary with the other operand constant along p (read
-// once per row run), 2 binary with any other strides, 3 as 1 with that
-// operand contiguous along q: its 32-value segment of each tile arrives in
-// the stage with the tile, by a bulk copy on the same mbarrier (no global
-// load waits at the start of a tile).
+// once per row run; the values of the warp's next tile are loaded while the
+// current one is processed, so no tile starts by waiting on them), 2 binary
+// with any other strides.
 template <class Op, class TC, class TA, class TB, class TO, int NIN, int BMODE, int BOXB>
 __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_constant__ CUtensorMap tm, Op op,
                                                                   const TB* __restrict__ b, TO* __restrict__ out,
@@ -149,13 +145,9 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
   constexpr int PASSES = kTmaRows / (RB * E);
   constexpr int STAGES = tma_stages(BOXB);
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
-  // other operand's segment per stage, padded so every stage (a TMA
-  // destination) stays 128-byte aligned
-  constexpr int BSEG = BMODE == 3 ? (kTmaRows * (int)sizeof(TBv) + 127) / 128 * 128 : 0;
   constexpr int TILE = kTmaRows * BOXB;
-  constexpr int STAGE = TILE + BSEG;
+  constexpr int STAGE = TILE;
   static_assert(CH <= 32 && PASSES >= 1, "tile shape does not fit the lane layout");
-  static_assert(BSEG % 16 == 0, "segment must keep stages 16-byte aligned");
   extern __shared__ char tma_smem[];
   const uint32_t base = (smem_u32(tma_smem) + 127u) & ~127u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -169,19 +161,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
     const TileIdx x = tma_tile(t, ti);
     const uint32_t bar = bars + 8u * (uint32_t)s;
     const uint32_t dst = stages + (uint32_t)(s * STAGE);
-    uint32_t bbytes = 0;
-    if constexpr (BMODE == 3) {
-      // the segment's values along q (fewer on the last tile row; the
-      // host checked that every segment is a whole number of 16 bytes)
-      const int64_t q0 = x.tq * kTmaRows;
-      const int64_t nq = t.dq - q0 < kTmaRows ? t.dq - q0 : kTmaRows;
-      bbytes = nq > 0 ? (uint32_t)(nq * (int64_t)sizeof(TBv)) : 0u;
-    }
-    mbar_expect_tx(bar, TILE + bbytes);
+    mbar_expect_tx(bar, TILE);
     tma_load_tile(dst, &tm, t.batched, (int)(x.tp * PX), (int)(x.tq * kTmaRows), (int)x.bi, bar);
-    if constexpr (BMODE == 3) {
-      if (bbytes) bulk_load(dst + TILE, reinterpret_cast<const TBv*>(b) + x.tq * kTmaRows, bbytes, bar);
-    }
   };
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(bars + 8u * (uint32_t)s, 1);
@@ -196,6 +177,24 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
   // 16-byte loads are conflict-free without a swizzle.
   const int c = lane % CH;
   const int qb = lane / CH;
+  // BMODE 1: the other operand along q for every pass of a tile; `bq_next`
+  // holds the warp's next tile's values, loaded one tile ahead
+  constexpr int BQ = NIN == 2 && BMODE == 1 ? PASSES : 1;
+  TC bq_all[BQ][E], bq_next[BQ][E];
+  auto load_bq = [&](int64_t tile_index, TC (&dstv)[BQ][E]) {
+    if constexpr (NIN == 2 && BMODE == 1) {
+      const TileIdx y = tma_tile(t, tile_index);
+      const TBv* bb = reinterpret_cast<const TBv*>(b) + y.bi * t.bsb;
+      const int64_t qy = y.tq * kTmaRows;
+#pragma unroll
+      for (int pass = 0; pass < PASSES; ++pass) {
+        const int64_t q = qy + (pass * RB + qb) * E;
+#pragma unroll
+        for (int k2 = 0; k2 < E; ++k2) dstv[pass][k2] = q < t.dq ? cvt<TC>(bb[(q + k2) * t.sb_q]) : TC{};
+      }
+    }
+  };
+  load_bq(gw, bq_next);
   for (int64_t k = 0;; ++k) {
     const int64_t ti = gw + k * nw;
     if (ti >= t.ntiles) break;
@@ -208,27 +207,13 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
     const uint32_t tile = stages + (uint32_t)(s * STAGE);
     const int64_t p0 = x.tp * PX + c * E, q0 = x.tq * kTmaRows;
     TO* ob = out + x.bi * t.bso;
-    // the other operand along q for every pass, loaded up front so that
-    // their latencies overlap (one wait per tile, not one per pass)
-    TC bq_all[NIN == 2 && (BMODE == 1 || BMODE == 3) ? PASSES : 1][E];
-    if constexpr (NIN == 2 && BMODE == 3) {
-      const char* seg = tma_smem + (tile + TILE - smem_u32(tma_smem));
-#pragma unroll
-      for (int pass = 0; pass < PASSES; ++pass) {
-        const int r0 = (pass * RB + qb) * E;
-#pragma unroll
-        for (int k2 = 0; k2 < E; ++k2)
-          bq_all[pass][k2] = q0 + r0 < t.dq ? cvt<TC>(reinterpret_cast<const TBv*>(seg)[r0 + k2]) : TC{};
-      }
-    }
     if constexpr (NIN == 2 && BMODE == 1) {
-      const TBv* bb = reinterpret_cast<const TBv*>(b) + x.bi * t.bsb;
+      // this tile's values (loaded one tile ago), then the next tile's
 #pragma unroll
-      for (int pass = 0; pass < PASSES; ++pass) {
-        const int64_t q = q0 + (pass * RB + qb) * E;
+      for (int pass = 0; pass < PASSES; ++pass)
 #pragma unroll
-        for (int k2 = 0; k2 < E; ++k2) bq_all[pass][k2] = q < t.dq ? cvt<TC>(bb[(q + k2) * t.sb_q]) : TC{};
-      }
+        for (int k2 = 0; k2 < E; ++k2) bq_all[pass][k2] = bq_next[pass][k2];
+      if (ti + nw < t.ntiles) load_bq(ti + nw, bq_next);
     }
 #pragma unroll
     for (int pass = 0; pass < PASSES; ++pass) {
@@ -251,7 +236,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32) k_ew_tiled_tma(const __grid_co
             const TC av = cvt<TC>(reinterpret_cast<const TA*>(&v[k2])[j]);
             if constexpr (NIN == 2) {
               TC bv;
-              if constexpr (BMODE == 1 || BMODE == 3) {
+              if constexpr (BMODE == 1) {
                 bv = bq_all[pass][k2];
               } else {
                 bv = cvt<TC>(reinterpret_cast<const TBv*>(b)[x.bi * t.bsb + p * t.sb_p + (q + k2) * t.sb_q]);
@@ -328,13 +313,6 @@ int launch_tiled_tma(const Op& op, const TA* a, const TB* b, TO* out, const Tile
   if constexpr (NIN == 1) {
     return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 1, 0, BOXB>, tma_smem_bytes(BOXB));
   } else {
-    constexpr int BSEG = (kTmaRows * (int)sizeof(TB) + 127) / 128 * 128;
-    // the other operand contiguous along q, 16-byte aligned, every tile's
-    // segment (32 values, fewer on the last tile row) a whole number of
-    // 16-byte units: it rides in the stages
-    if (ta.sb_p == 0 && ta.sb_q == 1 && !t.batched && (kTmaRows * (int)sizeof(TB)) % 16 == 0 &&
-        ((uintptr_t)b & 15) == 0 && (ta.dq * (int64_t)sizeof(TB)) % 16 == 0)
-      return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 3, BOXB>, tma_smem_bytes(BOXB, BSEG));
     if (ta.sb_p == 0) return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 1, BOXB>, tma_smem_bytes(BOXB));
     return launch(k_ew_tiled_tma<Op, TC, TA, TB, TO, 2, 2, BOXB>, tma_smem_bytes(BOXB));
   }
