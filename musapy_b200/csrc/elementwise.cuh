@@ -86,6 +86,12 @@ template <class Op, class = void>
 struct IsPaired : std::false_type {};
 template <class Op>
 struct IsPaired<Op, std::void_t<decltype(Op::kPaired)>> : std::bool_constant<Op::kPaired> {};
+// Paired ops whose fast path can run on every pair, with a range test for a
+// fix-up afterwards (pair_fast / pair_ok).
+template <class Op, class = void>
+struct HasFastPair : std::false_type {};
+template <class Op>
+struct HasFastPair<Op, std::void_t<decltype(std::declval<const Op&>().pair_ok(float2{}))>> : std::true_type {};
 // Ops with much arithmetic per element (transcendentals, pow).
 template <class Op, class = void>
 struct IsHeavy : IsPaired<Op> {};
@@ -134,30 +140,38 @@ MPB_D void apply_pack(const Op& op, const VPack<TA, N>& pa, const VPack<TBv, N>&
 }
 
 // ------------------------------------------------------------- EW_CONTIG
-// The loop is instantiated twice: without broadcast operands (the common
-// case, no per-element selects) and with them.
-template <bool BC, class Op, class TC, class TA, class TB, class TO, int NIN>
+// The loop is instantiated without broadcast operands (the common case, no
+// per-element selects) and with them, and with 32-bit indices when the
+// length allows (64-bit index arithmetic costs several instructions per
+// pack). The lanes of a warp run the loop's trips together (the warp's first
+// lane decides), so a warp-wide vote inside a trip is safe: unary ops with a
+// fast paired path run it on every pair and fix the rare out-of-range
+// elements up after one vote, instead of a branch per pair.
+template <bool BC, class Op, class TC, class TA, class TB, class TO, int NIN, class IdxT>
 MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restrict__ b, TO* __restrict__ out,
-                       int64_t n, int a_bc_in, int b_bc_in) {
+                       IdxT n, int a_bc_in, int b_bc_in) {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
+  using AP = Apply<Op, TC, TO, NIN>;
   constexpr int N = ew_pack<TA, TBv, TO>();
   constexpr int UNR = 4;
+  constexpr bool kVote = AP::kPair && HasFastPair<Op>::value && N % 2 == 0 && !BC;
   const bool a_bc = BC && a_bc_in;
   const bool b_bc = BC && b_bc_in;
-  const int64_t nvec = n / N;
-  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
+  const IdxT nvec = n / N;
+  const IdxT lane = threadIdx.x & 31;
+  const IdxT gtid = (IdxT)blockIdx.x * blockDim.x + threadIdx.x;
+  const IdxT gstride = (IdxT)gridDim.x * blockDim.x;
   const TA a0 = a_bc ? a[0] : TA{};
   TBv b0{};
   if constexpr (NIN == 2) {
     if (b_bc) b0 = b[0];
   }
-  for (int64_t v = gtid; v < nvec; v += gstride * UNR) {
+  for (IdxT v = gtid; v - lane < nvec; v += gstride * UNR) {
     VPack<TA, N> pa[UNR];
     VPack<TBv, N> pb[UNR];
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      const int64_t vi = v + u * gstride;
+      const IdxT vi = v + u * gstride;
       if (vi < nvec) {
         if (!a_bc) vload<TA, N, true>(pa[u], a + vi * N);
         if constexpr (NIN == 2) {
@@ -165,17 +179,56 @@ MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restr
         }
       }
     }
+    if constexpr (kVote) {
+      bool ok = true;
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const int64_t vi = v + u * gstride;
-      if (vi < nvec) {
-        VPack<TO, N> po;
-        apply_pack<Op, TC, TO, NIN>(op, pa[u], pb[u], a_bc, b_bc, a0, b0, po);
-        vstore<TO, N>(out + vi * N, po);
+      for (int u = 0; u < UNR; ++u) {
+        const IdxT vi = v + u * gstride;
+        if (vi < nvec) {
+          VPack<TO, N> po;
+#pragma unroll
+          for (int j = 0; j < N; j += 2) {
+            const float2 x = make_float2(cvt<float>(pa[u][j]), cvt<float>(pa[u][j + 1]));
+            const float2 r = op.pair_fast(x);
+            ok = ok && op.pair_ok(x);
+            po[j] = cvt<TO>(r.x);
+            po[j + 1] = cvt<TO>(r.y);
+          }
+          vstore<TO, N>(out + vi * N, po);
+        }
+      }
+      if (!__all_sync(0xffffffffu, ok)) {
+        // rare: an argument outside the fast range; its pair is redone by
+        // the full form and rewritten by this same thread
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+          const IdxT vi = v + u * gstride;
+          if (vi < nvec) {
+#pragma unroll
+            for (int j = 0; j < N; j += 2) {
+              const float2 x = make_float2(cvt<float>(pa[u][j]), cvt<float>(pa[u][j + 1]));
+              if (!op.pair_ok(x)) {
+                const float2 r = op.pair(x);
+                out[vi * N + j] = cvt<TO>(r.x);
+                out[vi * N + j + 1] = cvt<TO>(r.y);
+              }
+            }
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const IdxT vi = v + u * gstride;
+        if (vi < nvec) {
+          VPack<TO, N> po;
+          apply_pack<Op, TC, TO, NIN>(op, pa[u], pb[u], a_bc, b_bc, a0, b0, po);
+          vstore<TO, N>(out + vi * N, po);
+        }
       }
     }
   }
-  const int64_t t = nvec * N + gtid;
+  const IdxT t = nvec * N + gtid;
   if (t < n) {
     const TA av = a_bc ? a0 : a[t];
     TBv bv{};
@@ -191,10 +244,14 @@ MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restr
 // hide its latency (pow f16 +24%, sin +15%, exp +7%), and a narrow input word
 // (bf16 -> f32 loads 8 bytes per pack) needs them to keep enough bytes in
 // flight (+17%).
+// The paired float transcendentals (sin/cos/exp) take a 3-block floor: 85
+// registers hold their packed constants and four packs in flight without
+// spilling, and three blocks of 256 threads still hide the arithmetic.
 template <class Op, class TA, class TB, class TO, int NIN>
 constexpr int ew_min_blocks() {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
   constexpr int N = ew_pack<TA, TBv, TO>();
+  if constexpr (IsPaired<Op>::value && std::is_same<TA, float>::value && std::is_same<TO, float>::value) return 3;
   return (IsHeavy<Op>::value || VPack<TA, N>::kBytes < 16) ? 4 : 1;
 }
 
@@ -202,10 +259,18 @@ template <class Op, class TC, class TA, class TB, class TO, int NIN>
 __global__ void __launch_bounds__(kEwThreads, ew_min_blocks<Op, TA, TB, TO, NIN>()) k_ew_contig(Op op, const TA* __restrict__ a,
                                                           const TB* __restrict__ b, TO* __restrict__ out,
                                                           int64_t n, int a_bc, int b_bc) {
+  // 32-bit indices while n and every index the loop forms stay below 2^31
+  const bool small = n < (int64_t(1) << 31) - (int64_t)gridDim.x * blockDim.x * 64;
   if (a_bc || b_bc) {
-    contig_loop<true, Op, TC, TA, TB, TO, NIN>(op, a, b, out, n, a_bc, b_bc);
+    if (small)
+      contig_loop<true, Op, TC, TA, TB, TO, NIN, uint32_t>(op, a, b, out, (uint32_t)n, a_bc, b_bc);
+    else
+      contig_loop<true, Op, TC, TA, TB, TO, NIN, int64_t>(op, a, b, out, n, a_bc, b_bc);
   } else {
-    contig_loop<false, Op, TC, TA, TB, TO, NIN>(op, a, b, out, n, 0, 0);
+    if (small)
+      contig_loop<false, Op, TC, TA, TB, TO, NIN, uint32_t>(op, a, b, out, (uint32_t)n, 0, 0);
+    else
+      contig_loop<false, Op, TC, TA, TB, TO, NIN, int64_t>(op, a, b, out, n, 0, 0);
   }
 }
 

@@ -155,6 +155,8 @@ MPB_D V exp_core(V x) {
 }
 
 MPB_D float expf_(float x) { return exp_in_range(x) ? exp_core(x) : expf_wide(x); }
+MPB_D bool exp_fast_ok(float2 x) { return exp_in_range(x.x) && exp_in_range(x.y); }
+MPB_D float2 expf2_fast(float2 x) { return exp_core(x); }
 MPB_D float2 expf2_(float2 x) {
   float2 v = exp_core(x);
   if (!(exp_in_range(x.x) && exp_in_range(x.y))) {
@@ -166,6 +168,25 @@ MPB_D float2 expf2_(float2 x) {
 
 // ------------------------------------------------------------------ sin/cos
 MPB_D bool trig_in_range(float x) { return fabsf(x) < 1048576.0f; }  // 2^20; false for NaN
+
+// The quadrant k mod 4 (the low bits of kb = k + 1.5 * 2^23; cos adds one)
+// selects cos r (odd) or sin r (even) and bit 1 of it flips the sign, done
+// with integer bit operations. sin r takes the sign of r: the two agree
+// except for r = -0, where the polynomial's +0 would lose it (sin(-0) = -0),
+// and for |x| < 2^-12 (k = 0, r = x) the polynomial already rounds to x.
+template <int COS, class V>
+MPB_D V trig_select(V kb, V r, V sv, V cv) {
+  V out;
+#pragma unroll
+  for (int i = 0; i < lanes_of(V{}); ++i) {
+    const unsigned q = (unsigned)__float_as_int(lane(kb, i)) + (unsigned)COS;
+    const unsigned sb = ((unsigned)__float_as_int(lane(sv, i)) & 0x7fffffffu) |
+                        ((unsigned)__float_as_int(lane(r, i)) & 0x80000000u);
+    const unsigned v = (q & 1u) ? (unsigned)__float_as_int(lane(cv, i)) : sb;
+    lane(out, i) = __int_as_float((int)(v ^ ((q & 2u) << 30)));
+  }
+  return out;
+}
 
 // sin (COS = 0) or cos (COS = 1) for |x| < 2^20.
 template <int COS, class V>
@@ -196,17 +217,7 @@ MPB_D V sincos_core(V x) {
   const V r2e = f_fma(s, s, f_mul(r2, splat<V>(-1.0f)));      // s*s - fl(s*s), exact
   const V tail = f_sub(corr, f_fma(splat<V>(0.5f), r2e, f_mul(s, rl)));
   const V cv = f_add(w, f_fma(f_mul(r2, r2), pc, tail));
-  V kbv = kb, xv = x, svv = sv, cvv = cv, out;
-#pragma unroll
-  for (int i = 0; i < lanes_of(V{}); ++i) {
-    const int q = __float_as_int(lane(kbv, i)) + COS;  // low bits: k mod 4
-    float v = (q & 1) ? lane(cvv, i) : lane(svv, i);
-    v = (q & 2) ? -v : v;
-    // sin x rounds to x for |x| < 2^-12; this also keeps the sign of -0
-    if (COS == 0 && fabsf(lane(xv, i)) < 0x1p-12f) v = lane(xv, i);
-    lane(out, i) = v;
-  }
-  return out;
+  return trig_select<COS>(kb, s, sv, cv);
 }
 
 // sin (COS = 0) or cos (COS = 1) for |x| < 2^15: r = x - k*pi/2 by three FMA
@@ -235,16 +246,7 @@ MPB_D V sincos_core_fast(V x) {
   const V corr = f_add(f_sub(splat<V>(1.0f), w), nh);       // its rounding error, exact
   const V r2e = f_fma(r, r, f_mul(r2, splat<V>(-1.0f)));    // r*r - fl(r*r), exact
   const V cv = f_add(w, f_fma(f_mul(r2, r2), pc, f_fma(splat<V>(-0.5f), r2e, corr)));
-  V kbv = kb, xv = x, svv = sv, cvv = cv, out;
-#pragma unroll
-  for (int i = 0; i < lanes_of(V{}); ++i) {
-    const int q = __float_as_int(lane(kbv, i)) + COS;  // low bits: k mod 4
-    float v = (q & 1) ? lane(cvv, i) : lane(svv, i);
-    v = (q & 2) ? -v : v;
-    if (COS == 0 && fabsf(lane(xv, i)) < 0x1p-12f) v = lane(xv, i);
-    lane(out, i) = v;
-  }
-  return out;
+  return trig_select<COS>(kb, r, sv, cv);
 }
 constexpr float kTrigFastBound = 32768.0f;  // 2^15
 
@@ -274,6 +276,12 @@ MPB_D float2 sincosf2_(float2 x) {
   if (fabsf(x.x) < kTrigFastBound && fabsf(x.y) < kTrigFastBound) return sincos_core_fast<COS>(x);
   return make_float2(sincosf_<COS>(x.x), sincosf_<COS>(x.y));
 }
+// The pair form's fast path alone and its range test, for kernels that run
+// the fast path on every pair and fix the rare out-of-range elements up
+// afterwards (one warp-wide test instead of a branch per pair).
+MPB_D bool trig_fast_ok(float2 x) { return fabsf(x.x) < kTrigFastBound && fabsf(x.y) < kTrigFastBound; }
+template <int COS>
+MPB_D float2 sincosf2_fast(float2 x) { return sincos_core_fast<COS>(x); }
 MPB_D float sinf_(float x) { return sincosf_<0>(x); }
 MPB_D float cosf_(float x) { return sincosf_<1>(x); }
 

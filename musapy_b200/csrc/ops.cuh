@@ -134,22 +134,31 @@ struct OpNeC {
 };
 
 // ------------------------------------------------------------------- unary
+// Paired ops also expose their fast path (`pair_fast`, no range branch) and
+// its range test (`pair_ok`); out-of-range pairs go through `pair`, whose
+// results are the same as the one-element form's.
 struct OpSin {
   static constexpr bool kPaired = true;
   MPB_D float operator()(float a) const { return mathf::sinf_(a); }
   MPB_D float2 pair(float2 a) const { return mathf::sincosf2_<0>(a); }
+  MPB_D float2 pair_fast(float2 a) const { return mathf::sincosf2_fast<0>(a); }
+  MPB_D bool pair_ok(float2 a) const { return mathf::trig_fast_ok(a); }
   MPB_D double operator()(double a) const { return sin(a); }
 };
 struct OpCos {
   static constexpr bool kPaired = true;
   MPB_D float operator()(float a) const { return mathf::cosf_(a); }
   MPB_D float2 pair(float2 a) const { return mathf::sincosf2_<1>(a); }
+  MPB_D float2 pair_fast(float2 a) const { return mathf::sincosf2_fast<1>(a); }
+  MPB_D bool pair_ok(float2 a) const { return mathf::trig_fast_ok(a); }
   MPB_D double operator()(double a) const { return cos(a); }
 };
 struct OpExp {
   static constexpr bool kPaired = true;
   MPB_D float operator()(float a) const { return mathf::expf_(a); }
   MPB_D float2 pair(float2 a) const { return mathf::expf2_(a); }
+  MPB_D float2 pair_fast(float2 a) const { return mathf::expf2_fast(a); }
+  MPB_D bool pair_ok(float2 a) const { return mathf::exp_fast_ok(a); }
   MPB_D double operator()(double a) const { return exp(a); }
 };
 struct OpLog {
