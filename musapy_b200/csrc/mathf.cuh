@@ -171,19 +171,19 @@ MPB_D bool trig_in_range(float x) { return fabsf(x) < 1048576.0f; }  // 2^20; fa
 
 // The quadrant k mod 4 (the low bits of kb = k + 1.5 * 2^23; cos adds one)
 // selects cos r (odd) or sin r (even) and bit 1 of it flips the sign, done
-// with integer bit operations. sin r takes the sign of r: the two agree
-// except for r = -0, where the polynomial's +0 would lose it (sin(-0) = -0),
-// and for |x| < 2^-12 (k = 0, r = x) the polynomial already rounds to x.
+// with integer bit operations. sin(+-0) is +-0: the reduction turns r = -0
+// into +0 (adding the +0 product k*C2 for k = 0), so a zero argument is
+// returned as is (every other |x| < 2^-12 already rounds to x).
 template <int COS, class V>
-MPB_D V trig_select(V kb, V r, V sv, V cv) {
+MPB_D V trig_select(V kb, V x, V sv, V cv) {
   V out;
 #pragma unroll
   for (int i = 0; i < lanes_of(V{}); ++i) {
     const unsigned q = (unsigned)__float_as_int(lane(kb, i)) + (unsigned)COS;
-    const unsigned sb = ((unsigned)__float_as_int(lane(sv, i)) & 0x7fffffffu) |
-                        ((unsigned)__float_as_int(lane(r, i)) & 0x80000000u);
-    const unsigned v = (q & 1u) ? (unsigned)__float_as_int(lane(cv, i)) : sb;
-    lane(out, i) = __int_as_float((int)(v ^ ((q & 2u) << 30)));
+    const unsigned v = (q & 1u) ? (unsigned)__float_as_int(lane(cv, i)) : (unsigned)__float_as_int(lane(sv, i));
+    float f = __int_as_float((int)(v ^ ((q & 2u) << 30)));
+    if (COS == 0 && lane(x, i) == 0.0f) f = lane(x, i);
+    lane(out, i) = f;
   }
   return out;
 }
@@ -217,7 +217,7 @@ MPB_D V sincos_core(V x) {
   const V r2e = f_fma(s, s, f_mul(r2, splat<V>(-1.0f)));      // s*s - fl(s*s), exact
   const V tail = f_sub(corr, f_fma(splat<V>(0.5f), r2e, f_mul(s, rl)));
   const V cv = f_add(w, f_fma(f_mul(r2, r2), pc, tail));
-  return trig_select<COS>(kb, s, sv, cv);
+  return trig_select<COS>(kb, x, sv, cv);
 }
 
 // sin (COS = 0) or cos (COS = 1) for |x| < 2^15: r = x - k*pi/2 by three FMA
@@ -246,7 +246,7 @@ MPB_D V sincos_core_fast(V x) {
   const V corr = f_add(f_sub(splat<V>(1.0f), w), nh);       // its rounding error, exact
   const V r2e = f_fma(r, r, f_mul(r2, splat<V>(-1.0f)));    // r*r - fl(r*r), exact
   const V cv = f_add(w, f_fma(f_mul(r2, r2), pc, f_fma(splat<V>(-0.5f), r2e, corr)));
-  return trig_select<COS>(kb, r, sv, cv);
+  return trig_select<COS>(kb, x, sv, cv);
 }
 constexpr float kTrigFastBound = 32768.0f;  // 2^15
 
