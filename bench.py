@@ -400,6 +400,7 @@ def run_b200(args) -> None:
     t_start.record(stream)
     for k in range(args.steps):
         step(evs[k])
+    sh.join_exchanges(dev)  # the last record exchanges end inside the timed region
     t_end.record(stream)
     torch.cuda.synchronize()
     launches = ms._lib.launch_count() - launches0
@@ -436,6 +437,7 @@ def run_b200(args) -> None:
         for d, h, n in copies_in:
             check(LIB.mpb_copy_h2d(d, h, n, sraw), "e2e input copy")
         step()
+        sh.join_exchanges(dev)
         for h, d, n in copies_out:
             check(LIB.mpb_copy_d2h(h, d, n, sraw), "e2e result copy")
     e1.record(stream)
@@ -447,7 +449,13 @@ def run_b200(args) -> None:
     # max over ranks of the step time, total bytes over ranks
     b_local = step_bytes(nloc, cols)
     vals = torch.tensor([ms_total / args.steps, e2e_ms], dtype=torch.float64, device=f"cuda:{dev}")
+    per_rank = None
     if world > 1:
+        mine = torch.tensor([ms_total / args.steps] + [op_ms[k] for k in ("add", "sum_axis1", "sum_all", "argmax")],
+                            dtype=torch.float64, device=f"cuda:{dev}")
+        allr = torch.empty((world, mine.numel()), dtype=torch.float64, device=f"cuda:{dev}")
+        dist.all_gather_into_tensor(allr, mine)
+        per_rank = [[round(v, 4) for v in r] for r in allr.cpu().tolist()]
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     t_step, t_e2e = float(vals[0]), float(vals[1])
     total_bytes = sum(step_bytes(rows, cols).values())
@@ -501,6 +509,11 @@ def run_b200(args) -> None:
         "gpu_launches": int(launches),
         "clocks": clk,
     }
+    if per_rank is not None:
+        line["config"]["per_rank_ms"] = {"columns": ["step", "add", "sum_axis1", "sum_all", "argmax"],
+                                         "ranks": per_rank,
+                                         "note": "device time per rank (CUDA events); ops on the main stream, "
+                                                 "the record exchanges overlap on a side stream"}
     if suite is not None:
         line["config"]["suite"] = suite
     if cpu is not None:

@@ -166,20 +166,23 @@ MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restr
   if constexpr (NIN == 2) {
     if (b_bc) b0 = b[0];
   }
-  for (IdxT v = gtid; v - lane < nvec; v += gstride * UNR) {
-    VPack<TA, N> pa[UNR];
-    VPack<TBv, N> pb[UNR];
+  if constexpr (kVote) {
+    // Arithmetic-heavy ops: the next trip's packs are loaded before this
+    // trip's are computed, so the loads stay in flight through the compute
+    // (otherwise a warp has no loads outstanding while it computes).
+    VPack<TA, N> pa[UNR], pn[UNR];
+    auto load_trip = [&](IdxT v, VPack<TA, N>(&dst)[UNR]) {
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const IdxT vi = v + u * gstride;
-      if (vi < nvec) {
-        if (!a_bc) vload<TA, N, true>(pa[u], a + vi * N);
-        if constexpr (NIN == 2) {
-          if (!b_bc) vload<TBv, N, true>(pb[u], reinterpret_cast<const TBv*>(b) + vi * N);
-        }
+      for (int u = 0; u < UNR; ++u) {
+        const IdxT vi = v + u * gstride;
+        if (vi < nvec) vload<TA, N, true>(dst[u], a + vi * N);
       }
-    }
-    if constexpr (kVote) {
+    };
+    load_trip(gtid, pn);
+    for (IdxT v = gtid; v - lane < nvec; v += gstride * UNR) {
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) pa[u] = pn[u];
+      if (v + gstride * UNR - lane < nvec) load_trip(v + gstride * UNR, pn);
       bool ok = true;
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
@@ -216,7 +219,21 @@ MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restr
           }
         }
       }
-    } else {
+    }
+  } else {
+    for (IdxT v = gtid; v - lane < nvec; v += gstride * UNR) {
+      VPack<TA, N> pa[UNR];
+      VPack<TBv, N> pb[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const IdxT vi = v + u * gstride;
+        if (vi < nvec) {
+          if (!a_bc) vload<TA, N, true>(pa[u], a + vi * N);
+          if constexpr (NIN == 2) {
+            if (!b_bc) vload<TBv, N, true>(pb[u], reinterpret_cast<const TBv*>(b) + vi * N);
+          }
+        }
+      }
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
         const IdxT vi = v + u * gstride;

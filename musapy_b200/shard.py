@@ -105,6 +105,10 @@ class PeerExchange:
             raise errors.InteropError("peer exchange: a rank could not map the other ranks' buffers")
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+        # The fused exchanges run here, ordered after the local reduction by
+        # an event: the rank's next pass starts while its exchange waits for
+        # the other ranks (their records arrive over NVLink meanwhile).
+        self.side = torch.cuda.Stream(device=dev)
 
     def _release(self) -> None:
         with torch.cuda.device(self.dev):
@@ -135,7 +139,9 @@ class PeerExchange:
                                        self.status.data_ptr(), stream), "peer exchange")
 
     def check(self) -> None:
-        """Raise if any exchange gave up waiting for a rank (synchronises)."""
+        """Raise if any exchange gave up waiting for a rank (synchronises the
+        device, side stream included)."""
+        torch.cuda.synchronize(self.dev)
         if int(self.status.item()) != 0:
             raise errors.StreamError(f"peer exchange on cuda:{self.dev}: a rank did not arrive within the wait limit")
 
@@ -150,6 +156,27 @@ class PeerExchange:
             with torch.cuda.device(self.dev):
                 LIB.mpb_peer_free(self._buf)
             self._buf.value = None
+
+
+def _on_side(ex: PeerExchange, dev: int, outs, launch) -> None:
+    """Run `launch(stream_handle)` on the exchange's side stream after the
+    work queued so far on the current stream (the local reduction that wrote
+    the record), with the ms stream bookkeeping of the outputs `outs` (the
+    side stream waits for their earlier users and becomes their last user)."""
+    main = torch.cuda.current_stream(dev)
+    ex.side.wait_stream(main)
+    with torch.cuda.stream(ex.side):
+        handle = _streams.launch("sharded exchange", dev, *outs)
+        launch(handle)
+
+
+def join_exchanges(dev: int) -> None:
+    """Make the current stream of `dev` wait for every record exchange queued
+    so far (e.g. before timing ends or before reading results with torch)."""
+    main = torch.cuda.current_stream(dev)
+    for (d, _), ex in _EXCHANGES.items():
+        if d == dev and ex is not None:
+            main.wait_stream(ex.side)
 
 
 _EXCHANGES: dict = {}
@@ -208,12 +235,37 @@ def sum_axis(x: ShardedArray, axis: int, out: Array | None = None) -> ShardedArr
                         x.row0, x.group)
 
 
+class _Slots:
+    """Two alternating record slots: a slot is written by the local reduction
+    on the current stream only after the exchange that last read it (on the
+    side stream) is done."""
+
+    def __init__(self, dev: int, n: int, dtype) -> None:
+        self.buf = torch.zeros((2, n), dtype=dtype, device=f"cuda:{dev}")
+        self.read_done = [None, None]
+        self.k = 0
+
+    def next(self, dev: int) -> torch.Tensor:
+        self.k ^= 1
+        ev = self.read_done[self.k]
+        if ev is not None:
+            torch.cuda.current_stream(dev).wait_event(ev)
+        return self.buf[self.k]
+
+    def read_by(self, stream) -> None:
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.read_done[self.k] = ev
+
+
 class _SumCombine:
     """Scratch of a full sum/mean: the local f64 partial (first of two
-    doubles: the NCCL route all-reduces it in place) and the results."""
+    doubles: the NCCL route all-reduces it in place; the peer route
+    alternates between two slots) and the results."""
 
     def __init__(self, dev: int, out_dt: _dt.Dtype, world: int = 1) -> None:
         self.partial = torch.zeros(2, dtype=torch.float64, device=f"cuda:{dev}")
+        self.slots = _Slots(dev, 2, torch.float64)
         self.sum_out = empty((), out_dt, dev)
         self.mean_out = empty((), out_dt, dev)
 
@@ -234,19 +286,23 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
     nbytes = LIB.mpb_reduce_scratch_bytes(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code,
                                           mask, cd.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
+    ex = peer_exchange(dev, x.group)
+    partial = c.slots.next(dev) if ex is not None else c.partial
     if a.size == 0:  # a rank without rows (more ranks than rows) contributes 0
         with torch.cuda.stream(_streams.current_stream(dev).torch_stream):
-            c.partial.zero_()
+            partial.zero_()
     else:
         check(LIB.mpb_reduce(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code, mask,
-                             c.partial.data_ptr(), _dt.F64, cd.code, 1,
+                             partial.data_ptr(), _dt.F64, cd.code, 1,
                              scratch.data_ptr() if scratch is not None else None, nbytes, stream), "sum_all")
     world, _ = _world(x.group)
-    ex = peer_exchange(dev, x.group)
     if ex is not None:
-        # partials of all ranks over NVLink, summed in rank order on every rank
-        ex.sum_finalize(c.partial, float(x.global_size), a.dtype.code, c.sum_out.data_ptr, c.mean_out.data_ptr,
-                        stream)
+        # partials of all ranks over NVLink, summed in rank order on every
+        # rank, on the exchange's side stream
+        _on_side(ex, dev, (c.sum_out, c.mean_out),
+                 lambda h: ex.sum_finalize(partial, float(x.global_size), a.dtype.code, c.sum_out.data_ptr,
+                                           c.mean_out.data_ptr, h))
+        c.slots.read_by(ex.side)
         return c.sum_out, c.mean_out
     if world > 1:
         dist.all_reduce(c.partial, op=dist.ReduceOp.SUM, group=x.group)
@@ -258,6 +314,7 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
 class _ArgCombine:
     def __init__(self, dev: int, world: int) -> None:
         self.rec = torch.empty(2, dtype=torch.int64, device=f"cuda:{dev}")
+        self.slots = _Slots(dev, 2, torch.int64)
         self.all = torch.empty(2 * world, dtype=torch.int64, device=f"cuda:{dev}")
         self.index = empty((), _dt.int64, dev)
         self.value = torch.empty(1, dtype=torch.float64, device=f"cuda:{dev}")
@@ -280,21 +337,26 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
     nbytes = LIB.mpb_reduce_scratch_bytes(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
                                           src.dtype.code)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
+    ex = peer_exchange(dev, x.group)
+    rec = c.slots.next(dev) if ex is not None else c.rec
     if src.size == 0:  # a rank without rows sends the empty record {0, INT64_MAX}
         with torch.cuda.stream(_streams.current_stream(dev).torch_stream):
-            c.rec[0] = 0
-            c.rec[1] = np.iinfo(np.int64).max
+            rec[0] = 0
+            rec[1] = np.iinfo(np.int64).max
     else:
         # only the shard holding global element 0 applies the first-element NaN rule
         check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
-                             c.rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
+                             rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
                              scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
     is_int = src.dtype.code in (_dt.I64, _dt.U64)
-    ex = peer_exchange(dev, x.group)
     if ex is not None:
         row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
         starts = [shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)]
-        ex.arg_combine(c.rec, starts, is_max, is_int, c.index.data_ptr, c.value.data_ptr(), stream)
+        # c.value is a torch tensor outside the ms bookkeeping: torch users of
+        # it call join_exchanges first
+        _on_side(ex, dev, (c.index,),
+                 lambda h: ex.arg_combine(rec, starts, is_max, is_int, c.index.data_ptr, c.value.data_ptr(), h))
+        c.slots.read_by(ex.side)
         return c.index
     if world > 1:
         dist.all_gather_into_tensor(c.all, c.rec, group=x.group)

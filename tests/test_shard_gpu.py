@@ -54,10 +54,21 @@ def _worker(rank, world, port, x, row, out_q, transport="peer"):
     for _ in range(25):
         s2, _m2 = sh.sum_all(xs)
         seq.append((float(s2.item()), int(sh.argreduce_all(xs, True).item())))
+    # exchanges queued back to back with no host wait in between: x and -x
+    # alternate, each result copied on the current stream (ordered after the
+    # exchange by the stream bookkeeping) and read at the end
+    xn = sh.ShardedArray(ms.neg(xs.local), x.shape, r0)
+    queued = []
+    for i in range(30):
+        src = xs if i % 2 == 0 else xn
+        s3, _m3 = sh.sum_all(src)
+        a3 = sh.argreduce_all(src, True)
+        queued.append((ms.astype(s3, "f64"), ms.astype(a3, "i64")))
+    queued = [(float(v.item()), int(w.item())) for v, w in queued]
     for ex in sh._EXCHANGES.values():
         if ex is not None:
             ex.check()
-    out_q.put((rank, r0, r1, res, seq))
+    out_q.put((rank, r0, r1, res, seq, queued))
     sh.close_exchanges()
     dist.barrier(device_ids=[rank])
     dist.destroy_process_group()
@@ -91,7 +102,12 @@ def test_sharded_ops_two_gpus(oracle, case, transport):
     seqs = [[repr(t) for t in g[4]] for g in got]  # repr: NaN-safe comparison
     assert seqs[0] == seqs[1], "ranks disagree on repeated exchanges"
     assert len(set(seqs[0])) == 1, "repeated full reductions differ"
-    for rank, r0, r1, (y, rs, s, m, amax, amin), _ in got:
+    amax_neg = int(oracle.reduce("argmax", -x, None))
+    for rank, r0, r1, (y, rs, s, m, amax, amin), _, queued in got:
+        for i, (qs, qa) in enumerate(queued):
+            ws, wa = (s, amax) if i % 2 == 0 else (-s, amax_neg)
+            assert repr(qs) == repr(ws) and qa == wa, (case, transport, rank, i, qs, ws, qa, wa)
+    for rank, r0, r1, (y, rs, s, m, amax, amin), _, _q in got:
         assert_bits_equal(y, want_y[r0:r1], f"sharded add rank {rank}")
         want_rs = oracle.reduce("sum", want_y[r0:r1], axis=1)
         ok = np.abs(rs.astype(np.float64) - want_rs) <= 1e-5 * np.abs(want_y[r0:r1]).astype(np.float64).sum(1)
