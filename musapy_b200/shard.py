@@ -303,6 +303,9 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
                  lambda h: ex.sum_finalize(partial, float(x.global_size), a.dtype.code, c.sum_out.data_ptr,
                                            c.mean_out.data_ptr, h))
         c.slots.read_by(ex.side)
+        # a combine object made for this call alone is freed on return: its
+        # slots must outlive the side stream's read of them
+        c.slots.buf.record_stream(ex.side)
         return c.sum_out, c.mean_out
     if world > 1:
         dist.all_reduce(c.partial, op=dist.ReduceOp.SUM, group=x.group)
@@ -357,6 +360,8 @@ def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | N
         _on_side(ex, dev, (c.index,),
                  lambda h: ex.arg_combine(rec, starts, is_max, is_int, c.index.data_ptr, c.value.data_ptr(), h))
         c.slots.read_by(ex.side)
+        c.slots.buf.record_stream(ex.side)
+        c.value.record_stream(ex.side)
         return c.index
     if world > 1:
         dist.all_gather_into_tensor(c.all, c.rec, group=x.group)
