@@ -154,7 +154,11 @@ MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restr
   using AP = Apply<Op, TC, TO, NIN>;
   constexpr int N = ew_pack<TA, TBv, TO>();
   constexpr int UNR = 4;
+#ifndef MPB_EW_NO_VOTE
   constexpr bool kVote = AP::kPair && HasFastPair<Op>::value && N % 2 == 0 && !BC;
+#else
+  constexpr bool kVote = false;
+#endif
   const bool a_bc = BC && a_bc_in;
   const bool b_bc = BC && b_bc_in;
   const IdxT nvec = n / N;
@@ -178,11 +182,17 @@ MPB_D void contig_loop(const Op& op, const TA* __restrict__ a, const TB* __restr
         if (vi < nvec) vload<TA, N, true>(dst[u], a + vi * N);
       }
     };
+#ifndef MPB_EW_NO_PREFETCH
     load_trip(gtid, pn);
+#endif
     for (IdxT v = gtid; v - lane < nvec; v += gstride * UNR) {
+#ifndef MPB_EW_NO_PREFETCH
 #pragma unroll
       for (int u = 0; u < UNR; ++u) pa[u] = pn[u];
       if (v + gstride * UNR - lane < nvec) load_trip(v + gstride * UNR, pn);
+#else
+      load_trip(v, pa);
+#endif
       bool ok = true;
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
@@ -268,7 +278,11 @@ template <class Op, class TA, class TB, class TO, int NIN>
 constexpr int ew_min_blocks() {
   using TBv = typename std::conditional<NIN == 2, TB, TA>::type;
   constexpr int N = ew_pack<TA, TBv, TO>();
-  if constexpr (IsPaired<Op>::value && std::is_same<TA, float>::value && std::is_same<TO, float>::value) return 3;
+#ifndef MPB_EW_PAIRED_MINB
+#define MPB_EW_PAIRED_MINB 3
+#endif
+  if constexpr (IsPaired<Op>::value && std::is_same<TA, float>::value && std::is_same<TO, float>::value)
+    return MPB_EW_PAIRED_MINB;
   return (IsHeavy<Op>::value || VPack<TA, N>::kBytes < 16) ? 4 : 1;
 }
 
