@@ -539,13 +539,14 @@ __global__ void __launch_bounds__(256) k_ew_tiled(Op op, const TA* __restrict__ 
 // (the input's unit-stride dim), a transpose in registers, four 16-byte
 // stores along q - so a warp moves a 32 x 32 tile with eight vector accesses
 // per lane (the padded-tile kernel spends ~29 instructions per element on
-// scalar shared-memory traffic and index arithmetic). Per load instruction a
-// warp reads 8 rows x 64 bytes; per store it writes 4 rows x 128 bytes. A
-// block's 2 x 4 warps cover 64 (q) x 128 (p): 512 contiguous input bytes and
-// 256 contiguous output bytes per row. Blocks loop over the tiles (q
-// fastest) and load their next tile before storing the current one. Tiles
-// that reach past the array go element by element.
-constexpr int kReg4Q = 64, kReg4P = 128;
+// scalar shared-memory traffic and index arithmetic). Lane (qb, c), qb < 8,
+// c < 4, holds rows 4qb..4qb+3 of p-chunk c, so a warp covers 32 (q) x 16
+// (p); per load instruction it reads 8 rows x 64 bytes, per store it writes
+// 4 rows x 128 bytes. A block's 2 x 4 warps cover 64 (q) x 64 (p): 256
+// contiguous bytes per input row and per output row. Blocks loop over the
+// tiles (q fastest) and load their next tile before storing the current one.
+// Tiles that reach past the array go element by element.
+constexpr int kReg4Q = 64, kReg4P = 64;
 struct Reg4Args {
   int64_t dp, dq;         // extents along p and q
   int64_t sa_q, so_p;     // input stride along q, output stride along p (elements)
@@ -577,9 +578,9 @@ __global__ void __launch_bounds__(256) k_ew_tiled_reg4(Op op, const TA* __restri
       bi = x / t.ntp;
     }
     q0 = tq * kReg4Q + wq * 32;
-    p0 = tp * kReg4P + wp * 32;
+    p0 = tp * kReg4P + wp * 16;
   };
-  auto inside = [&](int64_t q0, int64_t p0) { return q0 + 32 <= t.dq && p0 + 32 <= t.dp; };
+  auto inside = [&](int64_t q0, int64_t p0) { return q0 + 32 <= t.dq && p0 + 16 <= t.dp; };
   auto load = [&](int64_t q0, int64_t p0, int64_t bi, uint4(&v)[4]) {
     const TA* base = a + bi * t.bsa + (q0 + 4 * qb) * t.sa_q + p0 + 4 * c;
 #pragma unroll
