@@ -534,108 +534,6 @@ __global__ void __launch_bounds__(256) k_ew_tiled(Op op, const TA* __restrict__ 
   }
 }
 
-// EW_TILED for 4-byte elements, unary (copies, casts, unary math), without
-// shared memory: each lane moves a 4 x 4 block - four 16-byte loads along p
-// (the input's unit-stride dim), a transpose in registers, four 16-byte
-// stores along q - so a warp moves a 32 x 32 tile with eight vector accesses
-// per lane (the padded-tile kernel spends ~29 instructions per element on
-// scalar shared-memory traffic and index arithmetic). Lane (qb, c), qb < 8,
-// c < 4, holds rows 4qb..4qb+3 of p-chunk c, so a warp covers 32 (q) x 16
-// (p); per load instruction it reads 8 rows x 64 bytes, per store it writes
-// 4 rows x 128 bytes. A block's 2 x 4 warps cover 64 (q) x 64 (p): 256
-// contiguous bytes per input row and per output row. Blocks loop over the
-// tiles (q fastest) and load their next tile before storing the current one.
-// Tiles that reach past the array go element by element.
-constexpr int kReg4Q = 64, kReg4P = 64;
-struct Reg4Args {
-  int64_t dp, dq;         // extents along p and q
-  int64_t sa_q, so_p;     // input stride along q, output stride along p (elements)
-  int64_t bsa, bso;       // batch strides (one batch dim at most)
-  int64_t ntq, ntp, ntiles;
-  FastDiv fd_ntq, fd_ntp;
-};
-
-template <class Op, class TC, class TA, class TO>
-__global__ void __launch_bounds__(256) k_ew_tiled_reg4(Op op, const TA* __restrict__ a, TO* __restrict__ out,
-                                                        Reg4Args t) {
-  static_assert(sizeof(TA) == 4 && sizeof(TO) == 4, "4-byte elements");
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = lane >> 2, c = lane & 3;
-  const int wq = warp >> 2, wp = warp & 3;
-  auto origin = [&](int64_t ti, int64_t& q0, int64_t& p0, int64_t& bi) {
-    int64_t tq, tp;
-    if (t.ntiles < 0xffffffffLL) {
-      uint32_t x, qq, rem;
-      t.fd_ntq.divmod((uint32_t)ti, x, rem);
-      tq = rem;
-      t.fd_ntp.divmod(x, qq, rem);
-      tp = rem;
-      bi = qq;
-    } else {
-      tq = ti % t.ntq;
-      const int64_t x = ti / t.ntq;
-      tp = x % t.ntp;
-      bi = x / t.ntp;
-    }
-    q0 = tq * kReg4Q + wq * 32;
-    p0 = tp * kReg4P + wp * 16;
-  };
-  auto inside = [&](int64_t q0, int64_t p0) { return q0 + 32 <= t.dq && p0 + 16 <= t.dp; };
-  auto load = [&](int64_t q0, int64_t p0, int64_t bi, uint4(&v)[4]) {
-    const TA* base = a + bi * t.bsa + (q0 + 4 * qb) * t.sa_q + p0 + 4 * c;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) v[k] = ld_stream16(base + k * t.sa_q);
-  };
-  int64_t ti = blockIdx.x;
-  if (ti >= t.ntiles) return;
-  int64_t q0, p0, bi;
-  origin(ti, q0, p0, bi);
-  bool have = inside(q0, p0);
-  uint4 cur[4], nxt[4];
-  if (have) load(q0, p0, bi, cur);
-  for (;;) {
-    const int64_t tn = ti + gridDim.x;
-    int64_t nq0 = 0, np0 = 0, nbi = 0;
-    bool nhave = false;
-    if (tn < t.ntiles) {
-      origin(tn, nq0, np0, nbi);
-      nhave = inside(nq0, np0);
-      if (nhave) load(nq0, np0, nbi, nxt);
-    }
-    if (have) {
-      TO* ob = out + bi * t.bso + (p0 + 4 * c) * t.so_p + q0 + 4 * qb;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 w;
-        TO* r = reinterpret_cast<TO*>(&w);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) r[k] = cvt<TO>(op(cvt<TC>(reinterpret_cast<const TA*>(&cur[k])[j])));
-        st_stream16(ob + j * t.so_p, w);
-      }
-    } else {
-      // an edge tile: element by element, the same lane layout
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int64_t q = q0 + 4 * qb + k;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int64_t p = p0 + 4 * c + j;
-          if (q < t.dq && p < t.dp)
-            out[bi * t.bso + p * t.so_p + q] = cvt<TO>(op(cvt<TC>(a[bi * t.bsa + q * t.sa_q + p])));
-        }
-      }
-    }
-    if (tn >= t.ntiles) break;
-    ti = tn;
-    q0 = nq0;
-    p0 = np0;
-    bi = nbi;
-    have = nhave;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
-  }
-}
-
 // ----------------------------------------------------------------- EW_ND
 constexpr int kNdEpt = 8;  // elements per thread per trip
 

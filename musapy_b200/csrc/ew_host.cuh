@@ -167,34 +167,6 @@ unsigned resident_grid(K kernel, int64_t items) {
   return (unsigned)(blocks < 1 ? 1 : blocks);
 }
 
-// The register-blocked form for unary ops on 4-byte elements; -1 (nothing
-// launched) when the layout does not allow its 16-byte accesses, or when
-// mpb_ew_set_tma(0) sends every transposed view to the padded-tile kernel.
-template <class Op, class TC, class TA, class TO>
-int run_tiled_reg4(const Op& op, const TA* a, TO* out, const TiledArgs& ta, cudaStream_t s) {
-  if (!tiled_tma_enabled()) return -1;
-  if (ta.nb > 1 || ((uintptr_t)a & 15) || ((uintptr_t)out & 15) || ta.sa_q <= 0 || ta.sa_q % 4 != 0 ||
-      ta.so_p % 4 != 0)
-    return -1;
-  if (ta.nb == 1 && (ta.bsa[0] % 4 != 0 || ta.bso[0] % 4 != 0)) return -1;
-  Reg4Args t;
-  t.dp = ta.dp;
-  t.dq = ta.dq;
-  t.sa_q = ta.sa_q;
-  t.so_p = ta.so_p;
-  t.bsa = ta.nb ? ta.bsa[0] : 0;
-  t.bso = ta.nb ? ta.bso[0] : 0;
-  const int64_t nbatch = ta.nb ? ta.bshape[0] : 1;
-  t.ntq = cdiv(ta.dq, kReg4Q);
-  t.ntp = cdiv(ta.dp, kReg4P);
-  t.ntiles = t.ntq * t.ntp * nbatch;
-  t.fd_ntq = FastDiv((uint32_t)(t.ntq < 0xffffffffLL ? t.ntq : 1));
-  t.fd_ntp = FastDiv((uint32_t)(t.ntp < 0xffffffffLL ? t.ntp : 1));
-  auto k = k_ew_tiled_reg4<Op, TC, TA, TO>;
-  k<<<resident_grid(k, t.ntiles), 256, 0, s>>>(op, a, out, t);
-  return launch_check("ew_tiled_reg4");
-}
-
 // TMA form with the second operand as the transposed one.
 template <class Op, class TC, class TA, class TB, class TO, int NIN>
 int run_tiled_tma_swapped(const Op& op, const TA* a, const TB* b, TO* out, const TiledArgs& t, cudaStream_t s) {
@@ -251,10 +223,6 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
         {
           const int rc = pl.tiled_op == 0 ? run_tiled_tma<Op, TC, TA, TB, TO, NIN>(op, a, b, out, t, s)
                                           : run_tiled_tma_swapped<Op, TC, TA, TB, TO, NIN>(op, a, b, out, t, s);
-          if (rc >= 0) return rc;
-        }
-        if constexpr (NIN == 1 && sizeof(TA) == 4 && sizeof(TO) == 4) {
-          const int rc = run_tiled_reg4<Op, TC, TA, TO>(op, a, out, t, s);
           if (rc >= 0) return rc;
         }
         tiled_count(t, tiled_edge<TC>());
