@@ -738,6 +738,18 @@ def run_suite(args) -> None:
         emit("C4", "mul c64 2^27", d["z1"].size * 24, lambda: ms.mul(z1, z2, out=z),
              cpu=(lambda: O.binary("mul", z1s, z2s), m * 24, "first 2^22 elements"))
         del z1, z2, z, d
+    if "SCAN" in cfgs:
+        # cumsum of 2^30 / scale f32 N(0,1): flattened (one decoupled look-back
+        # scan) and along rows of 4096 (one CTA per row)
+        n = (1 << 30) // args.scale
+        x = ms.empty((n,), "f32")
+        x.torch().normal_(generator=torch.Generator(device="cuda").manual_seed(1))
+        c = ms.cumsum(x)
+        emit("SCAN", f"cumsum axis=None f32 {n}", 8 * n, lambda: ms.cumsum(x, out=c))
+        xr = ms.reshape(x, (n // 4096, 4096))
+        cr = ms.cumsum(xr, axis=-1)
+        emit("SCAN", f"cumsum axis=-1 f32 ({n // 4096}, 4096)", 8 * n, lambda: ms.cumsum(xr, axis=-1, out=cr))
+        del x, c, xr, cr
     if "VIEWS" in cfgs:
         # contiguous() of transposed 16384^2 views (the padded-tile kernel for
         # 4-byte elements, TMA tiles for 2-byte ones); small enough to profile
@@ -976,7 +988,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-suite", action="store_true", help="skip the per-op table of the other workloads")
-    ap.add_argument("--suite", default="", help="comma list of C1..C4, VIEWS, NEXT: time every op of those configs")
+    ap.add_argument("--suite", default="", help="comma list of C1..C4, SCAN, VIEWS, NEXT: time every op of those configs")
     ap.add_argument("--scale", type=int, default=1,
                     help="with --suite: divide the large extents of C2-C4 by this power of two (profiling runs)")
     ap.add_argument("--suite-cpu", action="store_true",
