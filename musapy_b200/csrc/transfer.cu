@@ -139,15 +139,9 @@ Ring& ring() {
   return *r;
 }
 
-// Pinned slots and this device's events (lock held by the caller).
-int ring_ready(Ring& r, int dev) {
+// This device's events (lock held by the caller).
+int events_ready(Ring& r, int dev) {
   if (dev < 0 || dev >= kMaxDevices) return fail(MPB_ERR_INVALID, "copy: device %d out of range", dev);
-  if (r.host == nullptr) {
-    void* p = nullptr;
-    int rc = cuda_check(cudaHostAlloc(&p, (size_t)kSlots * kSlotBytes, cudaHostAllocPortable), "copy: cudaHostAlloc");
-    if (rc != MPB_OK) return rc;
-    r.host = static_cast<char*>(p);
-  }
   if (!r.ev_made[dev]) {
     for (int s = 0; s < kSlots; ++s) {
       int rc = cuda_check(cudaEventCreateWithFlags(&r.ev[dev][s], cudaEventDisableTiming), "copy: cudaEventCreate");
@@ -156,6 +150,18 @@ int ring_ready(Ring& r, int dev) {
     int rc = cuda_check(cudaEventCreateWithFlags(&r.direct[dev], cudaEventDisableTiming), "copy: cudaEventCreate");
     if (rc != MPB_OK) return rc;
     r.ev_made[dev] = true;
+  }
+  return MPB_OK;
+}
+
+// The pinned slots, allocated on the first staged copy (a copy between
+// page-locked memory and the device never needs them) - lock held.
+int ring_ready(Ring& r) {
+  if (r.host == nullptr) {
+    void* p = nullptr;
+    int rc = cuda_check(cudaHostAlloc(&p, (size_t)kSlots * kSlotBytes, cudaHostAllocPortable), "copy: cudaHostAlloc");
+    if (rc != MPB_OK) return rc;
+    r.host = static_cast<char*>(p);
   }
   return MPB_OK;
 }
@@ -202,8 +208,9 @@ int mpb_copy_h2d(void* dst, const void* src, size_t bytes, mpb_stream_t stream) 
   if (rc != MPB_OK) return rc;
   Ring& r = ring();
   std::lock_guard<std::mutex> lk(r.mu);
-  if ((rc = ring_ready(r, dev)) != MPB_OK) return rc;
+  if ((rc = events_ready(r, dev)) != MPB_OK) return rc;
   if (page_locked(src, bytes)) return direct_copy(r, dev, dst, src, bytes, cudaMemcpyHostToDevice, s);
+  if ((rc = ring_ready(r)) != MPB_OK) return rc;
   // slots may still be read by DMAs of a previous call: wait per slot below
   const size_t nchunks = (bytes + kSlotBytes - 1) / kSlotBytes;
   for (size_t k = 0; k < nchunks; ++k) {
@@ -230,8 +237,9 @@ int mpb_copy_d2h(void* dst, const void* src, size_t bytes, mpb_stream_t stream) 
   if (rc != MPB_OK) return rc;
   Ring& r = ring();
   std::lock_guard<std::mutex> lk(r.mu);
-  if ((rc = ring_ready(r, dev)) != MPB_OK) return rc;
+  if ((rc = events_ready(r, dev)) != MPB_OK) return rc;
   if (page_locked(dst, bytes)) return direct_copy(r, dev, dst, src, bytes, cudaMemcpyDeviceToHost, s);
+  if ((rc = ring_ready(r)) != MPB_OK) return rc;
   const size_t nchunks = (bytes + kSlotBytes - 1) / kSlotBytes;
   auto issue = [&](size_t k) -> int {
     const int slot = (int)(k % kSlots);
