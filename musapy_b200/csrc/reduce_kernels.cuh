@@ -610,8 +610,12 @@ __global__ void __launch_bounds__(kRedThreads) k_red_col(const typename P::In* _
 constexpr int kCombineBatch = 8;
 
 // Combine S partials per output. layout 0: [M][S] (row splits, a warp per
-// output); layout 1: [S][M] (column splits, a thread per output). Partials
-// are merged in split order, so results do not depend on scheduling.
+// output); layout 1: [S][M] (column splits, a thread per output); layout 2:
+// [M][S] with a CTA per output (row splits have few outputs: each thread
+// merges partials t, t + 256, ... - one round of loads for S <= 256 * k -
+// then the block reduces; a warp needed three dependent rounds of loads for
+// 592 partials). Every layout merges in a fixed order, so results do not
+// depend on scheduling.
 template <class P>
 __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::In* __restrict__ a, void* out,
                                                               const typename P::Acc* __restrict__ part, RedDev g,
@@ -639,6 +643,15 @@ __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::I
       const int64_t base = kept_off(g, o);
       acc = ext_zero_fix_warp<P>(acc, a + base, g, lane);
       if (lane == 0) write_out<P>(out, o, acc, ro, a + base);
+    }
+  } else if (layout == 2) {
+    for (int64_t o = blockIdx.x; o < g.M; o += gridDim.x) {
+      typename P::Acc acc = P::ident();
+      for (int j = threadIdx.x; j < S; j += blockDim.x) acc = P::merge(acc, part[o * S + j]);
+      acc = block_reduce<P>(acc);
+      const int64_t base = kept_off(g, o);
+      if (threadIdx.x < 32) acc = ext_zero_fix_warp<P>(acc, a + base, g, threadIdx.x);
+      if (threadIdx.x == 0) write_out<P>(out, o, acc, ro, a + base);
     }
   } else {
     const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -739,8 +752,8 @@ int launch_policy(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s)
       k_red_row_block<P><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, pl.chunk, vec, 1);
       int rc = launch_check("reduce_row_split");
       if (rc) return rc;
-      k_red_combine<P><<<blocks_for(pl.M * 32, kRedThreads, 32), kRedThreads, 0, s>>>(a, out, scratch, g, ro,
-                                                                                    (int)pl.splits, 0);
+      k_red_combine<P><<<(unsigned)(pl.M < 65535 ? pl.M : 65535), kRedThreads, 0, s>>>(a, out, scratch, g, ro,
+                                                                                    (int)pl.splits, 2);
       return launch_check("reduce_row_combine");
     }
     case RK_COL:

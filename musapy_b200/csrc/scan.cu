@@ -272,10 +272,12 @@ MPB_D Acc look_back(const unsigned long long* desc, int64_t tid, int64_t t, int*
     const int inc = __reduce_min_sync(0xffffffffu, my_inc);
     const int zero = __reduce_min_sync(0xffffffffu, my_zero);
     if (zero < inc) {  // a predecessor in front of the nearest prefix has not published yet
-      if (++spins > kSpinLimit) {
-        // give up: report it and use what is there (the result is then wrong
-        // and the status word says so)
+      // give up after the spin limit, or at once when another tile already
+      // gave up (the status word is non-zero): the result is then wrong and
+      // the status word says so, and no further tile waits out its limit
+      if (++spins > kSpinLimit || *(volatile int*)status != 0) {
         if (lane == 0) atomicOr(status, 1 << MPB_ERR_TIMEOUT);
+        spins = kSpinLimit + 1;
       } else {
         __nanosleep(ns);
         if (ns < 256) ns <<= 1;
@@ -411,6 +413,9 @@ __global__ void __launch_bounds__(kScanThreads, MPB_SCAN_SMEM_MINB)
   if (bulk_elems > 0 && !mbar_wait(bar, 0)) {
     if (threadIdx.x == 0) atomicOr(status, 1 << MPB_ERR_TIMEOUT);
   }
+  // a CTA whose copy never landed must not leave while it may still write
+  // into this CTA's shared memory: report it (above) and give its slot up
+  // only after the bounded wait, which is what mbar_wait did
   __syncthreads();
   // scan in place: thread-sequential over each vector, warp scan over lanes,
   // rows in order (the register tile's arithmetic)
