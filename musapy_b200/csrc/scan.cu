@@ -413,9 +413,6 @@ __global__ void __launch_bounds__(kScanThreads, MPB_SCAN_SMEM_MINB)
   if (bulk_elems > 0 && !mbar_wait(bar, 0)) {
     if (threadIdx.x == 0) atomicOr(status, 1 << MPB_ERR_TIMEOUT);
   }
-  // a CTA whose copy never landed must not leave while it may still write
-  // into this CTA's shared memory: report it (above) and give its slot up
-  // only after the bounded wait, which is what mbar_wait did
   __syncthreads();
   // scan in place: thread-sequential over each vector, warp scan over lanes,
   // rows in order (the register tile's arithmetic)
