@@ -476,157 +476,6 @@ __global__ void __launch_bounds__(kScanThreads, MPB_SCAN_SMEM_MINB)
   }
 }
 
-// The same scan with persistent CTAs and two tile buffers: a CTA takes its
-// next tile's ticket and issues that tile's bulk copy before it scans and
-// looks back for the current one, so the copy is in flight while the CTA
-// waits on its predecessors (the one-tile form has no load outstanding
-// then). Progress: a CTA publishes its current tile's aggregate before any
-// wait, and waits only on lower tickets; the lowest unpublished tile is
-// always a CTA's next tile whose current tile can finish.
-#ifndef MPB_SCAN_PIPE_MINB
-#define MPB_SCAN_PIPE_MINB 3
-#endif
-template <class Acc>
-__global__ void __launch_bounds__(kScanThreads, MPB_SCAN_PIPE_MINB)
-    k_scan_lookback_pipe(const Acc* __restrict__ a, Acc* __restrict__ out, ScanDev g, char* __restrict__ scratch,
-                         int64_t tiles_per_row) {
-  using ST = SmemTile<Acc>;
-  constexpr int VEC = ST::VEC;
-  extern __shared__ __align__(128) char scan_smem[];
-  __shared__ Acc s_warp[kScanThreads / 32];
-  __shared__ uint32_t s_ticket[2];
-  __shared__ Acc s_prefix;
-  __shared__ __align__(8) unsigned long long s_bar[2];
-  unsigned* ticket = reinterpret_cast<unsigned*>(scratch);
-  int* status = reinterpret_cast<int*>(scratch + 4);
-  unsigned long long* desc = reinterpret_cast<unsigned long long*>(scratch + 16);
-  const int64_t ntiles = g.M * tiles_per_row;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  Acc* bufs[2] = {reinterpret_cast<Acc*>(scan_smem), reinterpret_cast<Acc*>(scan_smem + kSmemTileBytes)};
-  const uint32_t bars[2] = {smem_u32(&s_bar[0]), smem_u32(&s_bar[1])};
-  // issue the copy of tile `tid` into buffer `b` (thread 0); returns the
-  // number of elements the bulk copy covers (the rest is loaded by threads)
-  auto tile_geo = [&](int64_t tid, const Acc*& in, Acc*& dst, int& cnt, int64_t& t) {
-    const int64_t row = tid / tiles_per_row;
-    t = tid - row * tiles_per_row;
-    int64_t oi, oo;
-    row_offsets(g, row, oi, oo);
-    const int64_t t0 = t * ST::kElems;
-    const int64_t n = g.L - t0;
-    cnt = n < ST::kElems ? (int)n : ST::kElems;
-    in = a + oi + t0;
-    dst = out + oo + t0;
-  };
-  auto issue = [&](int64_t tid, int b) {
-    const Acc* in;
-    Acc* dst;
-    int cnt;
-    int64_t t;
-    tile_geo(tid, in, dst, cnt, t);
-    const int bulk = cnt / VEC * VEC;
-    if (bulk > 0) {
-      mbar_expect_tx(bars[b], (uint32_t)(bulk * sizeof(Acc)));
-      bulk_load(smem_u32(bufs[b]), in, (uint32_t)(bulk * sizeof(Acc)), bars[b]);
-    }
-  };
-  if (threadIdx.x == 0) {
-    mbar_init(bars[0], 1);
-    mbar_init(bars[1], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_ticket[0] = atomicAdd(ticket, 1u);
-    if (s_ticket[0] < ntiles) issue(s_ticket[0], 0);
-  }
-  __syncthreads();
-  uint32_t phase[2] = {0u, 0u};
-  int b = 0;
-  for (;;) {
-    const int64_t tid = s_ticket[b];
-    if (tid >= ntiles) break;
-    // the next tile's ticket and copy first
-    if (threadIdx.x == 0) {
-      s_ticket[b ^ 1] = atomicAdd(ticket, 1u);
-      if (s_ticket[b ^ 1] < ntiles) issue(s_ticket[b ^ 1], b ^ 1);
-    }
-    const Acc* in;
-    Acc* dst;
-    int cnt;
-    int64_t t;
-    tile_geo(tid, in, dst, cnt, t);
-    Acc* tile = bufs[b];
-    const int bulk_elems = cnt / VEC * VEC;
-    for (int e = bulk_elems + threadIdx.x; e < ST::kElems; e += kScanThreads) tile[e] = e < cnt ? in[e] : Acc(0);
-    if (bulk_elems > 0) {
-      if (!mbar_wait(bars[b], phase[b]) && threadIdx.x == 0) atomicOr(status, 1 << MPB_ERR_TIMEOUT);
-      phase[b] ^= 1u;
-    }
-    __syncthreads();
-    const int wbase = warp * ST::kWarpElems;
-    Acc run = Acc(0);
-#pragma unroll 2
-    for (int j = 0; j < ST::J; ++j) {
-      Acc* p = tile + wbase + j * 32 * VEC + lane * VEC;
-      uint4 w = *reinterpret_cast<const uint4*>(p);
-      Acc* v = reinterpret_cast<Acc*>(&w);
-#pragma unroll
-      for (int k = 1; k < VEC; ++k) v[k] = sadd(v[k], v[k - 1]);
-      const Acc incl = warp_incl_scan<Acc>(v[VEC - 1], lane);
-      Acc excl = shfl_up<Acc>(incl, 1);
-      if (lane == 0) excl = Acc(0);
-      const Acc pre = sadd(run, excl);
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = sadd(v[k], pre);
-      *reinterpret_cast<uint4*>(p) = w;
-      run = sadd(run, shfl_idx<Acc>(incl, 31));
-    }
-    if (lane == 0) s_warp[warp] = run;
-    __syncthreads();
-    Acc wpre = Acc(0), total = Acc(0);
-    for (int w = 0; w < kScanThreads / 32; ++w) {
-      const Acc tw = s_warp[w];
-      if (w < warp) wpre = sadd(wpre, tw);
-      total = sadd(total, tw);
-    }
-    if (threadIdx.x < 32) {
-      if (t == 0) {
-        if (threadIdx.x == 0) {
-          desc_publish<Acc>(desc + 2 * tid, total, 2u);
-          s_prefix = Acc(0);
-        }
-      } else {
-        if (threadIdx.x == 0) desc_publish<Acc>(desc + 2 * tid, total, 1u);
-        const Acc excl = look_back<Acc>(desc, tid, t, status);
-        if (threadIdx.x == 0) {
-          desc_publish<Acc>(desc + 2 * tid, sadd(excl, total), 2u);
-          s_prefix = excl;
-        }
-      }
-    }
-    __syncthreads();
-    const Acc add = sadd(s_prefix, wpre);
-#pragma unroll 2
-    for (int j = 0; j < ST::J; ++j) {
-      const int e = wbase + j * 32 * VEC + lane * VEC;
-      uint4 w = *reinterpret_cast<const uint4*>(tile + e);
-      Acc* v = reinterpret_cast<Acc*>(&w);
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = sadd(v[k], add);
-      if (e + VEC <= cnt) {
-        st_stream16(dst + e, w);
-      } else {
-#pragma unroll
-        for (int k = 0; k < VEC; ++k)
-          if (e + k < cnt) dst[e + k] = v[k];
-      }
-    }
-    // the buffer is refilled by the copy issued in the next iteration: every
-    // thread's reads of it come first, then the proxy fence orders them
-    // before the asynchronous write
-    __syncthreads();
-    if (threadIdx.x == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    b ^= 1;
-  }
-}
-
 // ----------------------------------------------------------------- COLS
 // One thread per column (innermost kept dim unit-stride in and out).
 template <class In, class Acc>
@@ -761,24 +610,6 @@ int scan_typed(const ScanReq& r, cudaStream_t s, size_t* need_only) {
       const int64_t ntiles = g.M * pl.tiles_per_row;
       if constexpr (std::is_same<In, Acc>::value) {
         if (pl.smem) {
-#ifdef MPB_SCAN_PIPE
-          {
-            auto k = k_scan_lookback_pipe<Acc>;
-            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kSmemTileBytes) !=
-                cudaSuccess)
-              return cuda_check(cudaGetLastError(), "cumsum_lookback: shared memory size");
-            int per_sm = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kScanThreads, 2 * kSmemTileBytes) !=
-                    cudaSuccess ||
-                per_sm < 1)
-              per_sm = 1;
-            int64_t grid = (int64_t)sm_count() * per_sm;
-            if (grid > ntiles) grid = ntiles;
-            k<<<(unsigned)grid, kScanThreads, 2 * kSmemTileBytes, s>>>(a, out, g, static_cast<char*>(r.scratch),
-                                                                        pl.tiles_per_row);
-            return launch_check("cumsum_lookback_pipe");
-          }
-#endif
           if (cudaFuncSetAttribute(k_scan_lookback_smem<Acc>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kSmemTileBytes) != cudaSuccess)
             return cuda_check(cudaGetLastError(), "cumsum_lookback: shared memory size");
