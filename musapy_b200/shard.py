@@ -26,7 +26,7 @@ import torch.distributed as dist
 from . import dtypes as _dt
 from . import errors, ops
 from . import streams as _streams
-from ._lib import LIB, RED_OPS, check, i64arr
+from ._lib import LIB, NATIVE, RED_OPS, check, i64arr
 from .array import Array, empty
 
 
@@ -105,10 +105,14 @@ class PeerExchange:
             raise errors.InteropError("peer exchange: a rank could not map the other ranks' buffers")
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+        self._status_ptr = self.status.data_ptr()
         # The fused exchanges run here, ordered after the local reduction by
         # an event: the rank's next pass starts while its exchange waits for
         # the other ranks (their records arrive over NVLink meanwhile).
         self.side = torch.cuda.Stream(device=dev)
+        self.side_handle = self.side.cuda_stream
+        self.side_ms = _streams._wrap(dev, self.side)
+        self.ready = torch.cuda.Event()  # recorded on the main stream behind each local reduction
 
     def _release(self) -> None:
         with torch.cuda.device(self.dev):
@@ -122,21 +126,26 @@ class PeerExchange:
         check(LIB.mpb_peer_allgather(rec.data_ptr(), rec.nbytes, self._ptrs, self.rank, self.world, self.seq,
                                      out.data_ptr(), self.status.data_ptr(), stream), "peer exchange")
 
-    def sum_finalize(self, partial: torch.Tensor, count: float, out_dtype: int, sum_ptr: int, mean_ptr: int,
+    def sum_finalize(self, partial_ptr: int, count: float, out_dtype: int, sum_ptr: int, mean_ptr: int,
                      stream: int) -> None:
-        """Exchange the f64 partials and write the global sum and mean (one kernel)."""
+        """Exchange the f64 partials (`partial_ptr`: this rank's, on the device)
+        and write the global sum and mean (one kernel)."""
         self.seq += 1
-        check(LIB.mpb_peer_sum_finalize(partial.data_ptr(), self._ptrs, self.rank, self.world, self.seq, count,
-                                        out_dtype, sum_ptr, mean_ptr, self.status.data_ptr(), stream),
+        check(LIB.mpb_peer_sum_finalize(partial_ptr, self._ptrs, self.rank, self.world, self.seq, count,
+                                        out_dtype, sum_ptr, mean_ptr, self._status_ptr, stream),
               "peer exchange")
 
-    def arg_combine(self, rec: torch.Tensor, starts, is_max: bool, is_int: bool, index_ptr: int, value_ptr: int,
+    def arg_combine(self, rec_ptr: int, starts, is_max: bool, is_int: bool, index_ptr: int, value_ptr: int,
                     stream: int) -> None:
-        """Exchange the (value, index) records and write the global index (one kernel)."""
+        """Exchange the (value, index) records and write the global index (one
+        kernel); `starts`: the ranks' first flat indices (a list or an int64
+        ctypes array)."""
         self.seq += 1
-        check(LIB.mpb_peer_arg_combine(rec.data_ptr(), self._ptrs, self.rank, self.world, self.seq, i64arr(starts),
+        if isinstance(starts, (list, tuple)):
+            starts = i64arr(starts)
+        check(LIB.mpb_peer_arg_combine(rec_ptr, self._ptrs, self.rank, self.world, self.seq, starts,
                                        1 if is_max else 0, 1 if is_int else 0, index_ptr, value_ptr,
-                                       self.status.data_ptr(), stream), "peer exchange")
+                                       self._status_ptr, stream), "peer exchange")
 
     def check(self) -> None:
         """Raise if any exchange gave up waiting for a rank (synchronises the
@@ -161,13 +170,24 @@ class PeerExchange:
 def _on_side(ex: PeerExchange, dev: int, outs, launch) -> None:
     """Run `launch(stream_handle)` on the exchange's side stream after the
     work queued so far on the current stream (the local reduction that wrote
-    the record), with the ms stream bookkeeping of the outputs `outs` (the
-    side stream waits for their earlier users and becomes their last user)."""
+    the record), with the ms stream bookkeeping of the outputs `outs`: the
+    side stream waits for their users on other streams and becomes their last
+    user (in the steady state the side stream already is, and nothing but the
+    event is needed)."""
     main = torch.cuda.current_stream(dev)
-    ex.side.wait_stream(main)
-    with torch.cuda.stream(ex.side):
-        handle = _streams.launch("sharded exchange", dev, *outs)
-        launch(handle)
+    ex.ready.record(main)
+    ex.side.wait_event(ex.ready)
+    side = ex.side_ms
+    for o in outs:
+        buf = o._buf
+        last = getattr(buf, "_mpb_stream", None)
+        if last is side:
+            continue
+        if last is not None and last._handle != side._handle:
+            ex.side.wait_stream(last._torch)
+        buf.record_stream(ex.side)
+        buf._mpb_stream = side
+    launch(ex.side_handle)
 
 
 def join_exchanges(dev: int) -> None:
@@ -180,6 +200,7 @@ def join_exchanges(dev: int) -> None:
 
 
 _EXCHANGES: dict = {}
+_MISSING = object()
 
 
 def peer_exchange(dev: int, group=None) -> PeerExchange | None:
@@ -188,14 +209,16 @@ def peer_exchange(dev: int, group=None) -> PeerExchange | None:
     NCCL (MUSAPY_B200_SHARD_COLLECTIVE=nccl)."""
     import os
 
+    key = (dev, id(group))
+    ex = _EXCHANGES.get(key, _MISSING)
+    if ex is not _MISSING:
+        return ex
     world, _ = _world(group)
     if world <= 1 or os.environ.get("MUSAPY_B200_SHARD_COLLECTIVE", "peer") == "nccl":
         return None
     if dist.get_backend(group) != "nccl":  # CPU process groups (gloo) have no device buffers
+        _EXCHANGES[key] = None
         return None
-    key = (dev, id(group))
-    if key in _EXCHANGES:
-        return _EXCHANGES[key]
     try:
         ex = PeerExchange(dev, group)
     except errors.InteropError as e:  # every rank takes this branch together
@@ -242,20 +265,51 @@ class _Slots:
 
     def __init__(self, dev: int, n: int, dtype) -> None:
         self.buf = torch.zeros((2, n), dtype=dtype, device=f"cuda:{dev}")
-        self.read_done = [None, None]
+        self.views = [self.buf[0], self.buf[1]]
+        self.ptrs = [v.data_ptr() for v in self.views]
+        self.read_done = [torch.cuda.Event(), torch.cuda.Event()]
+        self.used = [False, False]
+        self.side_recorded = False
         self.k = 0
 
-    def next(self, dev: int) -> torch.Tensor:
+    def next(self, dev: int) -> int:
+        """Index of the slot to write next (the current stream waits for the
+        exchange that read it last)."""
         self.k ^= 1
-        ev = self.read_done[self.k]
-        if ev is not None:
-            torch.cuda.current_stream(dev).wait_event(ev)
-        return self.buf[self.k]
+        if self.used[self.k]:
+            torch.cuda.current_stream(dev).wait_event(self.read_done[self.k])
+        return self.k
 
-    def read_by(self, stream) -> None:
-        ev = torch.cuda.Event()
-        ev.record(stream)
-        self.read_done[self.k] = ev
+    def read_by(self, ex: PeerExchange) -> None:
+        self.read_done[self.k].record(ex.side)
+        self.used[self.k] = True
+        if not self.side_recorded:
+            # a combine object made for one call alone is freed on return:
+            # its slots must outlive the side stream's use of them
+            self.buf.record_stream(ex.side)
+            self.side_recorded = True
+
+
+class _Local:
+    """A local full reduction's plan and scratch, cached per layout (the
+    reduction runs on the current stream, so one scratch serves every call)."""
+
+    def __init__(self) -> None:
+        self.key = None
+        self.nbytes = 0
+        self.scratch = None
+        self.scratch_ptr = None
+
+    def prepare(self, dev: int, op: int, a: Array, in_code: int, mask: int, cd_code: int) -> None:
+        key = (op, a._shape, a._strides, in_code, mask, cd_code, a.data_ptr & 15)
+        if key == self.key:
+            return
+        n = NATIVE.reduce_scratch_bytes(op, a._shape, a._strides, a.data_ptr, in_code, mask, cd_code)
+        if n and (self.scratch is None or self.scratch.numel() < n):
+            self.scratch = torch.empty(n, dtype=torch.uint8, device=f"cuda:{dev}")
+            self.scratch_ptr = self.scratch.data_ptr()
+        self.nbytes = n
+        self.key = key
 
 
 class _SumCombine:
@@ -266,6 +320,7 @@ class _SumCombine:
     def __init__(self, dev: int, out_dt: _dt.Dtype, world: int = 1) -> None:
         self.partial = torch.zeros(2, dtype=torch.float64, device=f"cuda:{dev}")
         self.slots = _Slots(dev, 2, torch.float64)
+        self.local = _Local()
         self.sum_out = empty((), out_dt, dev)
         self.mean_out = empty((), out_dt, dev)
 
@@ -273,7 +328,9 @@ class _SumCombine:
 def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array, Array]:
     """Global sum and mean of a float array: local f32/f64 sum written as f64,
     one exchange of 8 bytes per rank (peer kernel with the finish fused, or
-    an NCCL all_reduce), mean over the true global element count."""
+    an NCCL all_reduce), mean over the true global element count. Pass the
+    same `combine` on every call of a loop: its plan, scratch and records are
+    reused (this call's host cost is part of every sharded step)."""
     a = x.local
     if a.dtype.code not in (_dt.F32, _dt.F64):
         raise errors.DtypeError("sum_all: float32/float64 shards only")
@@ -281,32 +338,30 @@ def sum_all(x: ShardedArray, combine: _SumCombine | None = None) -> tuple[Array,
     c = combine or _SumCombine(dev, a.dtype)
     cd = a.dtype
     mask = (1 << a.ndim) - 1
-    shape_c, strides_c = i64arr(a.shape), i64arr(a.strides)
+    op = RED_OPS["sum"]
     stream = _streams.current_stream(dev).cuda_stream
-    nbytes = LIB.mpb_reduce_scratch_bytes(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code,
-                                          mask, cd.code)
-    scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
     ex = peer_exchange(dev, x.group)
-    partial = c.slots.next(dev) if ex is not None else c.partial
+    if ex is not None:
+        k = c.slots.next(dev)
+        partial, partial_ptr = c.slots.views[k], c.slots.ptrs[k]
+    else:
+        partial, partial_ptr = c.partial, c.partial.data_ptr()
     if a.size == 0:  # a rank without rows (more ranks than rows) contributes 0
         with torch.cuda.stream(_streams.current_stream(dev).torch_stream):
             partial.zero_()
     else:
-        check(LIB.mpb_reduce(RED_OPS["sum"], a.ndim, shape_c, strides_c, a.data_ptr, a.dtype.code, mask,
-                             partial.data_ptr(), _dt.F64, cd.code, 1,
-                             scratch.data_ptr() if scratch is not None else None, nbytes, stream), "sum_all")
-    world, _ = _world(x.group)
+        c.local.prepare(dev, op, a, a.dtype.code, mask, cd.code)
+        check(NATIVE.reduce(op, a._shape, a._strides, a.data_ptr, a.dtype.code, mask, partial_ptr, _dt.F64, cd.code,
+                            1, c.local.scratch_ptr if c.local.nbytes else None, c.local.nbytes, stream), "sum_all")
     if ex is not None:
         # partials of all ranks over NVLink, summed in rank order on every
         # rank, on the exchange's side stream
         _on_side(ex, dev, (c.sum_out, c.mean_out),
-                 lambda h: ex.sum_finalize(partial, float(x.global_size), a.dtype.code, c.sum_out.data_ptr,
+                 lambda h: ex.sum_finalize(partial_ptr, float(x.global_size), a.dtype.code, c.sum_out.data_ptr,
                                            c.mean_out.data_ptr, h))
-        c.slots.read_by(ex.side)
-        # a combine object made for this call alone is freed on return: its
-        # slots must outlive the side stream's read of them
-        c.slots.buf.record_stream(ex.side)
+        c.slots.read_by(ex)
         return c.sum_out, c.mean_out
+    world, _ = _world(x.group)
     if world > 1:
         dist.all_reduce(c.partial, op=dist.ReduceOp.SUM, group=x.group)
     check(LIB.mpb_shard_sum_finalize(c.partial.data_ptr(), float(x.global_size), a.dtype.code,
@@ -318,61 +373,77 @@ class _ArgCombine:
     def __init__(self, dev: int, world: int) -> None:
         self.rec = torch.empty(2, dtype=torch.int64, device=f"cuda:{dev}")
         self.slots = _Slots(dev, 2, torch.int64)
+        self.local = _Local()
         self.all = torch.empty(2 * world, dtype=torch.int64, device=f"cuda:{dev}")
         self.index = empty((), _dt.int64, dev)
         self.value = torch.empty(1, dtype=torch.float64, device=f"cuda:{dev}")
+        self.value_ptr = self.value.data_ptr()
+        self.starts_key = None
+        self.starts = None
+        self.value_recorded = False
+
+    def rank_starts(self, x: ShardedArray, world: int):
+        """The ranks' first flat indices as an int64 ctypes array (cached)."""
+        a = x.local
+        row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
+        key = (x.global_shape, world, row_elems)
+        if key != self.starts_key:
+            self.starts = i64arr([shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)])
+            self.starts_key = key
+        return self.starts
 
 
 def argreduce_all(x: ShardedArray, is_max: bool = True, combine: _ArgCombine | None = None) -> Array:
     """Global argmax/argmin (flat index, first occurrence, musapy's NaN rule):
     local (value, index) record, one exchange of 16 bytes per rank (peer
     kernel with the combine fused, or an NCCL all_gather and a device
-    combine), in rank order."""
+    combine), in rank order. Pass the same `combine` on every call of a loop
+    (plan, scratch, records and rank offsets are reused)."""
     a = x.local
     dev = a._dev
     world, rank = _world(x.group)
     c = combine or _ArgCombine(dev, world)
     src = a if a.dtype.code in (_dt.F32, _dt.F64, _dt.F16, _dt.BF16, _dt.I64, _dt.U64) else ops.astype(a, _dt.int64)
     mask = (1 << src.ndim) - 1
-    shape_c, strides_c = i64arr(src.shape), i64arr(src.strides)
     stream = _streams.current_stream(dev).cuda_stream
     op = RED_OPS["argmax_rec" if is_max else "argmin_rec"]
-    nbytes = LIB.mpb_reduce_scratch_bytes(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
-                                          src.dtype.code)
-    scratch = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{dev}") if nbytes else None
     ex = peer_exchange(dev, x.group)
-    rec = c.slots.next(dev) if ex is not None else c.rec
+    if ex is not None:
+        k = c.slots.next(dev)
+        rec, rec_ptr = c.slots.views[k], c.slots.ptrs[k]
+    else:
+        rec, rec_ptr = c.rec, c.rec.data_ptr()
     if src.size == 0:  # a rank without rows sends the empty record {0, INT64_MAX}
         with torch.cuda.stream(_streams.current_stream(dev).torch_stream):
             rec[0] = 0
             rec[1] = np.iinfo(np.int64).max
     else:
         # only the shard holding global element 0 applies the first-element NaN rule
-        check(LIB.mpb_reduce(op, src.ndim, shape_c, strides_c, src.data_ptr, src.dtype.code, mask,
-                             rec.data_ptr(), _dt.I64, src.dtype.code, 1 if x.row0 == 0 else 0,
-                             scratch.data_ptr() if scratch is not None else None, nbytes, stream), "argreduce_all")
+        c.local.prepare(dev, op, src, src.dtype.code, mask, src.dtype.code)
+        check(NATIVE.reduce(op, src._shape, src._strides, src.data_ptr, src.dtype.code, mask, rec_ptr, _dt.I64,
+                            src.dtype.code, 1 if x.row0 == 0 else 0,
+                            c.local.scratch_ptr if c.local.nbytes else None, c.local.nbytes, stream), "argreduce_all")
     is_int = src.dtype.code in (_dt.I64, _dt.U64)
     if ex is not None:
-        row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
-        starts = [shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)]
+        starts = c.rank_starts(x, world)
         # c.value is a torch tensor outside the ms bookkeeping: torch users of
         # it call join_exchanges first
         _on_side(ex, dev, (c.index,),
-                 lambda h: ex.arg_combine(rec, starts, is_max, is_int, c.index.data_ptr, c.value.data_ptr(), h))
-        c.slots.read_by(ex.side)
-        c.slots.buf.record_stream(ex.side)
-        c.value.record_stream(ex.side)
+                 lambda h: ex.arg_combine(rec_ptr, starts, is_max, is_int, c.index.data_ptr, c.value_ptr, h))
+        c.slots.read_by(ex)
+        if not c.value_recorded:
+            c.value.record_stream(ex.side)
+            c.value_recorded = True
         return c.index
     if world > 1:
         dist.all_gather_into_tensor(c.all, c.rec, group=x.group)
         recs = c.all
-        row_elems = a.size // max(1, a.shape[0]) if a.ndim else 1
-        starts = [shard_rows(x.global_shape[0], world, r)[0] * row_elems for r in range(world)]
+        starts = c.rank_starts(x, world)
     else:
         recs = c.rec
-        starts = [0]
-    check(LIB.mpb_shard_arg_combine(recs.data_ptr(), world, i64arr(starts), 1 if is_max else 0, 1 if is_int else 0,
-                                    c.index.data_ptr, c.value.data_ptr(), stream), "argreduce_all")
+        starts = i64arr([0])
+    check(LIB.mpb_shard_arg_combine(recs.data_ptr(), world, starts, 1 if is_max else 0, 1 if is_int else 0,
+                                    c.index.data_ptr, c.value_ptr, stream), "argreduce_all")
     return c.index
 
 
