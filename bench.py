@@ -398,8 +398,10 @@ def run_b200(args) -> None:
     barrier()
     launches0 = ms._lib.launch_count()
     t_start.record(stream)
+    h0 = time.perf_counter()
     for k in range(args.steps):
         step(evs[k])
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to enqueue one step
     sh.join_exchanges(dev)  # the last record exchanges end inside the timed region
     t_end.record(stream)
     torch.cuda.synchronize()
@@ -504,6 +506,7 @@ def run_b200(args) -> None:
         "config": {"workload": WORKLOAD, "rows": rows, "cols": cols, "parallelism": f"axis0-shard{world}",
                    "global_batch": rows, "l2": "inputs 8 GiB > 126 MB L2: no flush needed",
                    "per_op_ms": {k: round(v, 4) for k, v in op_ms.items()},
+                   "host_enqueue_ms_per_step": round(host_ms, 4),
                    "per_op_gbs": {k: round(b_local[k] / (v * 1e-3) / 1e9, 1) for k, v in op_ms.items()},
                    "per_op_frac": {k: round(b_local[k] / (v * 1e-3) / 1e9 / peak, 4) for k, v in op_ms.items()}},
         "roofline": {"bound": "hbm", "kernel": "k_ew_rows (broadcast add)", "achieved": round(achieved, 1),
