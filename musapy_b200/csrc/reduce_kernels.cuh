@@ -506,8 +506,12 @@ __global__ void __launch_bounds__(kRedThreads) k_red_row_warp(const typename P::
 
 // ROW with a CTA per (output, split). When `partial`, CTA (sx, o) reduces
 // [sx*chunk, (sx+1)*chunk) of the single reduced dim into scratch[o*S + sx].
+// At most 56 registers a thread: a split grid is exactly one wave of 4 CTAs
+// per SM, and at 64 registers those 4 CTAs fill the register file, so any
+// small kernel running beside it (a sharded reduction's record exchange on
+// its side stream) pushed one CTA into a second wave.
 template <class P>
-__global__ void __launch_bounds__(kRedThreads) k_red_row_block(const typename P::In* __restrict__ a, void* out,
+__global__ void __maxnreg__(56) k_red_row_block(const typename P::In* __restrict__ a, void* out,
                                                                 typename P::Acc* __restrict__ scratch, RedDev g,
                                                                 RedOut ro, int64_t chunk, int vec, int partial) {
   constexpr int VEC = 16 / sizeof(typename P::In) > 0 ? 16 / sizeof(typename P::In) : 1;
