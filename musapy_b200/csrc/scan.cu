@@ -194,15 +194,17 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_rows(const In* __restrict
 // reader that sees the same flag in both words holds the value written with
 // it: no fence is needed between a value and its flag.
 //
-// Look-back (Merrill & Garland 2016, with a wide window): warp 0 reads the
+// Look-back (Merrill & Garland 2016, a warp-wide window): warp 0 reads the
 // descriptors of the kLookWindow tiles before this one in one round of loads
 // (kLookPerLane consecutive descriptors per lane), waits (bounded) until each
 // has a flag, finds the nearest inclusive prefix and adds it to the
 // aggregates in between; with none in the window it adds all of them and
 // moves the window back. Tiles take their index from an atomic ticket, so
-// every predecessor has started. The window is wide enough that the nearest
-// inclusive prefix lies inside it in the steady state: about (tiles started
-// per second) x (half an L2 round trip) tiles back.
+// every predecessor has started. One descriptor per lane (a 32-tile window,
+// one contiguous 512-byte load per round) is the fastest measured: a round
+// costs one L2 round trip whatever its width, but wider windows of 64, 128,
+// 256 and 512 tiles (2-16 loads per lane) made each round slower under the
+// scan's own traffic and the whole scan 4% to 2.1x slower.
 constexpr int64_t kSpinLimit = 1 << 22;  // polls per descriptor before giving up
 #ifndef MPB_SCAN_LB_J
 #define MPB_SCAN_LB_J 8
@@ -212,7 +214,10 @@ constexpr int64_t kSpinLimit = 1 << 22;  // polls per descriptor before giving u
 #endif
 constexpr int kLookJ = MPB_SCAN_LB_J;        // vector rows per warp of a look-back tile
 constexpr int kLookMinBlocks = MPB_SCAN_LB_MINB;  // CTAs per SM the registers must allow
-constexpr int kLookPerLane = 4;
+#ifndef MPB_SCAN_LB_PER_LANE
+#define MPB_SCAN_LB_PER_LANE 1
+#endif
+constexpr int kLookPerLane = MPB_SCAN_LB_PER_LANE;
 constexpr int kLookWindow = 32 * kLookPerLane;
 
 template <class Acc>
@@ -354,7 +359,10 @@ __global__ void __launch_bounds__(kScanThreads, kLookMinBlocks) k_scan_lookback(
 // in flight of the register tile, which is what a look-back scan's
 // bandwidth depends on (each tile waits for the predecessors between it and
 // the nearest published prefix).
-constexpr int kSmemTileBytes = 32768;
+#ifndef MPB_SCAN_SMEM_TILE
+#define MPB_SCAN_SMEM_TILE 32768
+#endif
+constexpr int kSmemTileBytes = MPB_SCAN_SMEM_TILE;
 #ifndef MPB_SCAN_SMEM_MINB
 #define MPB_SCAN_SMEM_MINB 6
 #endif
