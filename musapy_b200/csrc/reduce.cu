@@ -34,6 +34,12 @@ using red::cdiv;
 // Build the kept/reduced split. Reduced dims are ordered by decreasing
 // |stride| (the smallest innermost) and carry their logical C-order weight,
 // so any traversal still reports the reference's flat index.
+// Full and few-row reductions split each row into this many chunks per SM
+// (one wave of the split kernel at 4 CTAs per SM).
+#ifndef MPB_RED_SPLIT_PER_SM
+#define MPB_RED_SPLIT_PER_SM 4
+#endif
+
 int red_plan(const RedReq& r, RedPlan& pl) {
   if (r.ndim < 0 || r.ndim > MPB_MAX_DIMS) return fail(MPB_ERR_INVALID, "reduce: ndim %d out of range", r.ndim);
   pl = RedPlan();
@@ -163,7 +169,7 @@ int red_plan(const RedReq& r, RedPlan& pl) {
   if (row && pl.Li >= 32) {
     if (R == 1 && pl.M < 2 * sms && pl.L >= 65536) {
       pl.kind = RK_ROW_SPLIT;
-      int64_t S = cdiv(4 * sms, pl.M);
+      int64_t S = cdiv((int64_t)MPB_RED_SPLIT_PER_SM * sms, pl.M);
       int64_t max_s = pl.L / 16384;
       if (r.scratch_cap > 0 && max_s > (int64_t)(r.scratch_cap / (16 * (size_t)pl.M)))
         max_s = (int64_t)(r.scratch_cap / (16 * (size_t)pl.M));

@@ -338,16 +338,18 @@ int run_tiled_tma(const Op& op, const TA* a, const TB* b, TO* out, const TiledAr
       return -1;
     int* err = tiled_wait_flag();
     if (!err) return -1;
-    // Box width and tile grouping per element size, from a sweep on B200
-    // (16384^2 2-byte transpose, 8192^2 int64-transposed + float64 row):
-    // 2-byte elements 256-byte boxes in 4 x 1 groups (179 us, the
-    // shared-memory tile kernel 382 us); 8-byte elements 128-byte boxes in
-    // 2 x 2 groups (185 us vs 188 us). For 4-byte elements the
-    // shared-memory tile kernel stays faster (362 us vs 388 us at best).
+    // Box width and tile grouping per element size, from sweeps on B200
+    // (16384^2 2- and 4-byte transposes, 8192^2 int64-transposed + float64
+    // row; boxes of 64 / 128 / 256 bytes, groups of 1 x 4 / 2 x 2 / 4 x 1
+    // tiles, groups numbered q- or p-fastest): 2-byte elements 256-byte
+    // boxes in 4 x 1 groups (178 us, the shared-memory tile kernel 382 us);
+    // 8-byte elements 128-byte boxes in 4 x 1 groups (179 us; 2 x 2 groups
+    // 185 us, 256-byte boxes 193-199 us). For 4-byte elements the
+    // shared-memory tile kernel stays faster (362 us vs 390 us at best).
     if constexpr (SZ == 2) {
       return launch_tiled_tma<Op, TC, TA, TB, TO, NIN, 256, 2>(op, a, b, out, ta, err, s);
     } else if constexpr (SZ == 8) {
-      return launch_tiled_tma<Op, TC, TA, TB, TO, NIN, 128, 1>(op, a, b, out, ta, err, s);
+      return launch_tiled_tma<Op, TC, TA, TB, TO, NIN, 128, 2>(op, a, b, out, ta, err, s);
     } else {
       return -1;
     }
