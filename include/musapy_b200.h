@@ -87,6 +87,16 @@ int mpb_collapse(int ndim, const int64_t* shape, int nops, const int64_t* stride
 int mpb_reduce_plan(int ndim, const int64_t* shape, const int64_t* strides, int in_dtype, uint64_t axes_mask,
                     int64_t* M, int64_t* L, int64_t* splits);
 
+/* mpb_reduce_plan for reduction `op` (an mpb_red_op) of an input at address
+ * `a` (the column kernels' vector width depends on the op and on the
+ * address's alignment), also giving the outputs each thread of a column
+ * kernel (kinds 4 and 5) reduces: 1, or 2/4/8 when every group of them is
+ * one aligned 8- or 16-byte load at every reduced step. No counterpart in
+ * the reference (its column kernels take one output per thread). Host only;
+ * `a` is not dereferenced. */
+int mpb_reduce_plan_at(int op, int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype,
+                       uint64_t axes_mask, int64_t* M, int64_t* L, int64_t* splits, int* outputs_per_thread);
+
 /* ------------------------------------------------------------ elementwise */
 
 /* out = op(a[, b]) over `shape`, for every mpb_ew_op:

@@ -66,6 +66,9 @@ def _load() -> ctypes.CDLL:
     L.mpb_collapse.argtypes = [ctypes.c_int, c_i64p, ctypes.c_int, c_i64p, c_i64p, c_i64p]
     L.mpb_reduce_plan.restype = ctypes.c_int
     L.mpb_reduce_plan.argtypes = [ctypes.c_int, c_i64p, c_i64p, ctypes.c_int, ctypes.c_uint64, c_i64p, c_i64p, c_i64p]
+    L.mpb_reduce_plan_at.restype = ctypes.c_int
+    L.mpb_reduce_plan_at.argtypes = [ctypes.c_int, ctypes.c_int, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_int,
+                                     ctypes.c_uint64, c_i64p, c_i64p, c_i64p, ctypes.POINTER(ctypes.c_int)]
     L.mpb_elementwise.restype = ctypes.c_int
     L.mpb_elementwise.argtypes = [
         ctypes.c_int, ctypes.c_int, c_i64p,

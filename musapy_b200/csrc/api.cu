@@ -176,14 +176,14 @@ int mpb_collapse(int ndim, const int64_t* shape, int nops, const int64_t* stride
 }
 
 // Kind of kernel the reduction planner picks (RedKind), for host tests.
-int mpb_reduce_plan(int ndim, const int64_t* shape, const int64_t* strides, int in_dtype, uint64_t axes_mask,
-                    int64_t* M, int64_t* L, int64_t* splits) {
+int mpb_reduce_plan_at(int op, int ndim, const int64_t* shape, const int64_t* strides, const void* a, int in_dtype,
+                       uint64_t axes_mask, int64_t* M, int64_t* L, int64_t* splits, int* outputs_per_thread) {
   RedReq r{};
-  r.op = MPB_R_SUM;
+  r.op = op;
   r.ndim = ndim;
   r.shape = shape;
   r.strides = strides;
-  r.a = nullptr;
+  r.a = a;
   r.in_dt = in_dtype;
   r.axes_mask = axes_mask;
   r.allow_split = 1;
@@ -193,7 +193,13 @@ int mpb_reduce_plan(int ndim, const int64_t* shape, const int64_t* strides, int 
   if (M) *M = pl.M;
   if (L) *L = pl.L;
   if (splits) *splits = pl.splits;
+  if (outputs_per_thread) *outputs_per_thread = pl.colv;
   return pl.kind;
+}
+
+int mpb_reduce_plan(int ndim, const int64_t* shape, const int64_t* strides, int in_dtype, uint64_t axes_mask,
+                    int64_t* M, int64_t* L, int64_t* splits) {
+  return mpb_reduce_plan_at(MPB_R_SUM, ndim, shape, strides, nullptr, in_dtype, axes_mask, M, L, splits, nullptr);
 }
 
 int mpb_elementwise(int op, int ndim, const int64_t* shape, const void* a, int a_dtype, const int64_t* a_strides,

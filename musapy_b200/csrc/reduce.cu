@@ -188,6 +188,28 @@ int red_plan(const RedReq& r, RedPlan& pl) {
     }
   } else if (col || (row && pl.Li < 32)) {
     pl.kind = RK_COL;
+    // V adjacent outputs per thread with one 8- or 16-byte load per reduced
+    // step: one reduced dim, unit-stride kept inner dim, every V-group of
+    // outputs contiguous and aligned at every step. Arg reductions of 2- and
+    // 4-byte types take 8-byte loads: their fold (value, index, first-taken
+    // test) is longer, and twice the threads hide it better (argmax over
+    // axis 1 of (64, 4096, 4096) f32: 0.61 ms with 2 outputs per thread,
+    // 0.72 ms with 4); the other reductions take 16-byte loads (sum over
+    // axis 0: 0.624 ms with 4 per thread, 0.627 ms with 2).
+    const bool arg = r.op == MPB_R_ARGMAX || r.op == MPB_R_ARGMIN || r.op == MPB_R_ARGMAX_REC ||
+                     r.op == MPB_R_ARGMIN_REC;
+    const int max_load = arg && esz <= 4 ? 8 : 16;
+    if (R == 1 && col && esz >= 2 && esz <= 8) {
+      for (int v = max_load / esz; v >= 2 && v * esz >= 8; v >>= 1) {
+        bool ok = kshape[K - 1] % v == 0 && rst[0] % v == 0 && ((uintptr_t)r.a % (uintptr_t)(v * esz)) == 0;
+        for (int d = 0; d < K - 1 && ok; ++d)
+          if (kst[d] % v != 0) ok = false;
+        if (ok) {
+          pl.colv = v;
+          break;
+        }
+      }
+    }
     // Thread per output: a block of 256 outputs walks its whole chunk of the
     // reduced dim, so a block's time is proportional to the chunk length and
     // the pass takes ceil(w) "waves" of w = blocks * S / capacity. Splitting
@@ -197,13 +219,20 @@ int red_plan(const RedReq& r, RedPlan& pl) {
     //   data_bytes * ceil(w) / w + 32 * M * S
     // with capacity = 6 blocks per SM (the column kernels use <= 40 registers)
     // and chunks of at least 64 elements.
-    const int64_t blocks = cdiv(pl.M, 256);
-    const double cap = 6.0 * sms;
+    //
+    // With V outputs per thread (k_red_col_v, 4 blocks per SM) a grid that
+    // fits in one wave runs at full bandwidth as long as its loads in flight
+    // (128 bytes per thread) cover the memory latency, so such a grid with
+    // at least kColInflight bytes in flight is not split.
+    const int64_t blocks = cdiv(cdiv(pl.M, pl.colv), 256);
+    const double cap = (pl.colv > 1 ? 4.0 : 6.0) * sms;
     const double data = (double)pl.M * (double)pl.L * (double)esz;
     int64_t s_max = pl.L / 64;
     if (s_max > 4096) s_max = 4096;
     if (r.scratch_cap > 0 && s_max > (int64_t)(r.scratch_cap / (16 * (size_t)pl.M)))
       s_max = (int64_t)(r.scratch_cap / (16 * (size_t)pl.M));
+    constexpr double kColInflight = 8.0 * 1024 * 1024;
+    if (pl.colv > 1 && (double)blocks <= cap && (double)(pl.M / pl.colv) * 128.0 >= kColInflight) s_max = 1;
     int64_t best_s = 1;
     double best_cost = 0.0;
     for (int64_t S = 1; S <= (s_max > 1 ? s_max : 1); ++S) {

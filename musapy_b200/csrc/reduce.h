@@ -38,6 +38,7 @@ struct RedPlan {
   bool vectorized = false;
   int64_t splits = 1;
   int64_t chunk = 0;
+  int colv = 1;  // COL kinds: adjacent outputs per thread (one 8- or 16-byte load per reduced step)
 };
 
 int red_plan(const RedReq& r, RedPlan& pl);

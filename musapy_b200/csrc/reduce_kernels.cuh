@@ -611,6 +611,69 @@ __global__ void __launch_bounds__(kRedThreads) k_red_col(const typename P::In* _
   }
 }
 
+// COL with V adjacent outputs per thread (one reduced dim; the plan checks
+// that every group of V outputs is contiguous and V * sizeof(In)-aligned at
+// every reduced step): each step reads the V inputs as one 8- or 16-byte
+// load, and each output folds its elements in index order exactly as
+// k_red_col does. Fewer, wider loads and V times fewer threads: the argmax
+// over axis 1 of (64, 4096, 4096) f32 takes 131,072 threads (2 outputs
+// each), one partial wave with 16 MiB of loads in flight - no column split
+// and no merge pass.
+template <class P, int V>
+__global__ void __launch_bounds__(kRedThreads, 4) k_red_col_v(const typename P::In* __restrict__ a, void* out,
+                                                               typename P::Acc* __restrict__ scratch, RedDev g,
+                                                               RedOut ro, int64_t chunk, int partial) {
+  using In = typename P::In;
+  using Acc = typename P::Acc;
+  constexpr int B = V * (int)sizeof(In);
+  static_assert(B == 8 || B == 16, "8- or 16-byte loads");
+  using W = typename std::conditional<B == 16, uint4, uint2>::type;
+  constexpr int UNR = B == 16 ? 8 : 16;
+  const int sx = blockIdx.y;
+  const int64_t f0 = partial ? (int64_t)sx * chunk : 0;
+  int64_t f1 = partial ? f0 + chunk : g.L;
+  if (f1 > g.L) f1 = g.L;
+  const int64_t groups = g.M / V;
+  const int64_t st = g.rst[0], w = g.rw[0];
+  const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t q = gt; q < groups; q += gs) {
+    const int64_t o = q * V;
+    const int64_t base = kept_off(g, o);
+    Acc acc[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) acc[k] = P::ident();
+    const In* ap = a + base + f0 * st;
+    int64_t f = f0;
+    for (; f + UNR <= f1; f += UNR, ap += UNR * st) {
+      W v[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) v[u] = __ldcs(reinterpret_cast<const W*>(ap + u * st));
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        In e[V];
+        memcpy(e, &v[u], B);
+#pragma unroll
+        for (int k = 0; k < V; ++k) P::fold_seq(acc[k], e[k], (f + u) * w);
+      }
+    }
+    for (; f < f1; ++f, ap += st) {
+      const W v = __ldcs(reinterpret_cast<const W*>(ap));
+      In e[V];
+      memcpy(e, &v, B);
+#pragma unroll
+      for (int k = 0; k < V; ++k) P::fold_seq(acc[k], e[k], f * w);
+    }
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      if (partial)
+        scratch[(int64_t)sx * g.M + o + k] = acc[k];
+      else
+        write_out<P>(out, o + k, ext_zero_fix_thread<P>(acc[k], a + base + k, g), ro, a + base + k);
+    }
+  }
+}
+
 constexpr int kCombineBatch = 8;
 
 // Combine S partials per output. layout 0: [M][S] (row splits, a warp per
@@ -728,6 +791,44 @@ inline RedDev dev_of(const RedPlan& pl) {
   return g;
 }
 
+// k_red_col_v at the plan's vector width (only the widths whose loads are 8
+// or 16 bytes of In are instantiated; the plan picks no other).
+template <class P>
+int launch_col_v(const typename P::In* a, void* out, typename P::Acc* scratch, const RedDev& g, RedOut ro,
+                 const RedPlan& pl, int partial, cudaStream_t s) {
+  constexpr int SZ = (int)sizeof(typename P::In);
+  const int64_t groups = pl.M / pl.colv;
+  dim3 grid(partial ? (unsigned)cdiv(groups, kRedThreads) : (unsigned)blocks_for(groups, kRedThreads, 64),
+            partial ? (unsigned)pl.splits : 1u);
+  const int64_t chunk = partial ? pl.chunk : 0;
+  bool launched = false;
+  if constexpr (SZ == 2) {
+    if (pl.colv == 8) {
+      k_red_col_v<P, 8><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      launched = true;
+    } else if (pl.colv == 4) {
+      k_red_col_v<P, 4><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      launched = true;
+    }
+  } else if constexpr (SZ == 4) {
+    if (pl.colv == 4) {
+      k_red_col_v<P, 4><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      launched = true;
+    } else if (pl.colv == 2) {
+      k_red_col_v<P, 2><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      launched = true;
+    }
+  } else if constexpr (SZ == 8) {
+    if (pl.colv == 2) {
+      k_red_col_v<P, 2><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      launched = true;
+    }
+  }
+  if (!launched)
+    return fail(MPB_ERR_INVALID, "reduce: no column kernel for %d outputs of %d bytes per thread", pl.colv, SZ);
+  return launch_check(partial ? "reduce_col_v_split" : "reduce_col_v");
+}
+
 template <class P>
 int launch_policy(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s) {
   using In = typename P::In;
@@ -761,12 +862,18 @@ int launch_policy(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s)
       return launch_check("reduce_row_combine");
     }
     case RK_COL:
+      if (pl.colv > 1) return launch_col_v<P>(a, out, scratch, g, ro, pl, 0, s);
       k_red_col<P><<<blocks_for(pl.M, kRedThreads, 64), kRedThreads, 0, s>>>(a, out, scratch, g, ro, 0, 0);
       return launch_check("reduce_col");
     case RK_COL_SPLIT: {
-      dim3 grid((unsigned)cdiv(pl.M, kRedThreads), (unsigned)pl.splits);
-      k_red_col<P><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, pl.chunk, 1);
-      int rc = launch_check("reduce_col_split");
+      int rc;
+      if (pl.colv > 1) {
+        rc = launch_col_v<P>(a, out, scratch, g, ro, pl, 1, s);
+      } else {
+        dim3 grid((unsigned)cdiv(pl.M, kRedThreads), (unsigned)pl.splits);
+        k_red_col<P><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, pl.chunk, 1);
+        rc = launch_check("reduce_col_split");
+      }
       if (rc) return rc;
       k_red_combine<P><<<blocks_for(pl.M, kRedThreads, 64), kRedThreads, 0, s>>>(a, out, scratch, g, ro,
                                                                                (int)pl.splits, 1);

@@ -465,6 +465,115 @@ def test_reduce_strided_views(ms, oracle):
                          oracle.reduce("sum", np.abs(v).astype(np.float64), axis), 1e-5)
 
 
+def _col_plan(ms, a, axis, op="sum"):
+    """(kind, splits, outputs per thread) the planner picks for reduction `op`
+    of array `a` over `axis`."""
+    import ctypes
+
+    from musapy_b200._lib import LIB
+
+    n = a.ndim
+    M, L, S = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    v = ctypes.c_int()
+    code = {"sum": 0, "max": 2, "argmax": 5, "argmin": 6}[op]
+    kind = LIB.mpb_reduce_plan_at(code, n, (ctypes.c_int64 * n)(*a.shape), (ctypes.c_int64 * n)(*a.strides),
+                                  ctypes.c_void_p(a.data_ptr), a.dtype.code, 1 << axis, ctypes.byref(M),
+                                  ctypes.byref(L), ctypes.byref(S), ctypes.byref(v))
+    return kind, S.value, v.value
+
+
+# (dtype, shape, axis, view): views slice the kept inner dim so the base
+# moves by one element (narrower loads or one output per thread) or flip the
+# reduced axis (negative reduced stride)
+COL_V_CASES = [
+    (np.float32, (301, 256), 0, None), (np.float32, (301, 256), 0, "shift1"), (np.float32, (301, 256), 0, "shift2"),
+    (np.float32, (301, 256), 0, "flip"), (np.float32, (9, 333, 64), 1, None), (np.float32, (20000, 64), 0, None),
+    (np.float64, (301, 256), 0, None), (np.float64, (301, 256), 0, "shift1"), (np.float16, (301, 256), 0, None),
+    (np.float16, (301, 256), 0, "shift2"), (np.int64, (301, 256), 0, None),
+]
+
+
+@pytest.mark.parametrize("dtype,shape,axis,view", COL_V_CASES)
+def test_reduce_columns_several_outputs_per_thread(ms, oracle, dtype, shape, axis, view):
+    """Column reductions whose threads take 2, 4 or 8 adjacent outputs with
+    one 8- or 16-byte load per reduced step (and the one-per-thread kernel
+    where a view's alignment rules that out), split and unsplit, against the
+    oracle: max/min/argmax/argmin bit-exact (NaN first in a column, NaN
+    later, signed zeros, ties), sums and means within 1e-5 * sum|x| (1e-3 for
+    f16 results; bit-exact where the column is not split: the CPU path's
+    order)."""
+    rng = np.random.default_rng(41)
+    x = rand(rng, shape, dtype)
+    if np.dtype(dtype).kind == "f":
+        idx = (slice(None),) * axis
+        x[idx + (0, 3)] = np.nan            # NaN first in column 3
+        x[idx + (5, 4)] = np.nan            # NaN later in column 4
+        x[idx + (slice(None), 6)] = 0.0
+        x[idx + (7, 6)] = -0.0              # zero extremum: sign of the first zero
+        x[idx + (slice(None), 9)] = 2.0     # ties: the first index wins
+    def viewed(a):
+        """(device view, host array) of `a` under this case's view."""
+        d = dev(ms, a)
+        if view == "shift1":
+            return d[..., 1:253], a[..., 1:253]
+        if view == "shift2":
+            return d[..., 2:254], a[..., 2:254]
+        if view == "flip":
+            return ms.flip(d, axis=axis), np.flip(a, axis=axis)
+        return d, a
+
+    xd, ref = viewed(x)
+    size = np.dtype(dtype).itemsize
+    kind, splits, per_thread = _col_plan(ms, xd, axis)
+    kind_arg, _, per_thread_arg = _col_plan(ms, xd, axis, "argmax")
+    assert kind in (4, 5) and kind_arg in (4, 5)
+    if view is None:
+        assert per_thread == 16 // size
+        assert per_thread_arg == (8 if size <= 4 else 16) // size
+    for op in ("max", "min", "argmax", "argmin"):
+        if np.dtype(dtype) == np.float16 and op in ("max", "min"):
+            want = oracle.reduce(op, ref, axis).astype(np.float16)
+        else:
+            want = oracle.reduce(op, ref, axis)
+        assert_bits_equal(getattr(ms, op)(xd, axis=axis).numpy(), want,
+                          f"{op} {view} {per_thread_arg if op.startswith('arg') else per_thread}/thread")
+    half = np.dtype(dtype) == np.float16
+    cd, clean = viewed(np.nan_to_num(x))
+    for op in ("sum", "mean"):
+        got = getattr(ms, op)(cd, axis=axis).numpy()
+        # f16 sums accumulate in f32 on both sides and round once to f16
+        want = oracle.reduce(op, clean, axis)
+        want = want.astype(np.float16) if half else want
+        if (np.dtype(dtype).kind == "i" and op == "sum") or (np.dtype(dtype).kind == "f" and splits == 1):
+            assert_bits_equal(got, want, f"{op} {view} unsplit")
+        else:
+            L = clean.shape[axis]
+            bound = oracle.reduce("sum", np.abs(clean).astype(np.float64), axis) / (L if op == "mean" else 1)
+            assert_sum_close(got.astype(np.float64) if half else got, want.astype(np.float64) if half else want,
+                             bound, 1e-3 if half else 1e-5, f"{op} {view}")
+
+
+def test_reduce_columns_split_with_several_outputs_per_thread(ms, oracle):
+    """Few columns and a long reduced dim: the planner splits the column
+    kernel (4 outputs per thread, 2 for arg reductions), and the merge keeps
+    the first occurrence across splits."""
+    rng = np.random.default_rng(42)
+    x = rng.standard_normal((100000, 1024)).astype(np.float32)
+    x[99990, 7] = 50.0
+    x[10, 7] = 50.0                          # tie across splits: index 10 wins
+    x[0, 11] = np.nan
+    xd = dev(ms, x)
+    kind, splits, per_thread = _col_plan(ms, xd, 0)
+    assert (kind, per_thread) == (5, 4) and splits > 1
+    kind, splits, per_thread = _col_plan(ms, xd, 0, "argmax")
+    assert (kind, per_thread) == (5, 2) and splits > 1
+    for op in ("max", "min", "argmax", "argmin"):
+        assert_bits_equal(getattr(ms, op)(xd, axis=0).numpy(), oracle.reduce(op, x, 0), op)
+    y = np.nan_to_num(x)
+    got = ms.sum(dev(ms, y), axis=0).numpy()
+    assert_sum_close(got, oracle.reduce("sum", y, 0), oracle.reduce("sum", np.abs(y).astype(np.float64), 0), 1e-5)
+
+
 # ---------------------------------------------------------------- cumsum
 CUMSUM_CASES = [((4,), 0), ((2, 2), None), ((2, 2), 0), ((2, 2), 1), ((3, 70000), 1), ((1300,), 0), ((1537,), 0),
                 ((100_000,), 0), ((262, 4096), 1), ((64, 33, 5), 1), ((5000, 7), 0), ((1 << 21,), None),
