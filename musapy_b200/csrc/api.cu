@@ -36,6 +36,12 @@ int launch_check(const char* what) {
   return cuda_check(g_preserve_last_error ? cudaPeekAtLastError() : cudaGetLastError(), what);
 }
 
+int launch_check_pdl(cudaError_t e, const char* what) {
+  const int rc = launch_check(what);
+  if (rc) return rc;
+  return cuda_check(e, what);
+}
+
 int sm_count() {
   static int cache[64] = {0};
   int dev = 0;

@@ -6,10 +6,45 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <utility>
 #include "mpb_types.h"
 
 #define MPB_HD __host__ __device__ __forceinline__
 #define MPB_D __device__ __forceinline__
+
+// Programmatic dependent launch. The streaming elementwise and reduction
+// kernels are launched with launch_pdl, which lets the GPU start launching
+// the next kernel of the stream while this one finishes, and each such
+// kernel begins with pdl_enter: it lets its own dependents launch once all
+// of its CTAs have started, then waits until the kernel before it in the
+// stream has completed and its writes are visible. No global memory is
+// touched before that wait, so stream order holds exactly as without it;
+// what is saved is the launch latency between back-to-back kernels. After a
+// kernel launched the ordinary way the wait returns at once.
+MPB_D void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+#ifdef MPB_NO_PDL
+  cfg.numAttrs = 0;
+#else
+  cfg.numAttrs = 1;
+#endif
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 namespace mpb {
 

@@ -290,6 +290,7 @@ template <class Op, class TC, class TA, class TB, class TO, int NIN>
 __global__ void __launch_bounds__(kEwThreads, ew_min_blocks<Op, TA, TB, TO, NIN>()) k_ew_contig(Op op, const TA* __restrict__ a,
                                                           const TB* __restrict__ b, TO* __restrict__ out,
                                                           int64_t n, int a_bc, int b_bc) {
+  pdl_enter();
   // 32-bit indices while n and every index the loop forms stay below 2^31
   const bool small = n < (int64_t(1) << 31) - (int64_t)gridDim.x * blockDim.x * 64;
   if (a_bc || b_bc) {
@@ -394,6 +395,7 @@ __global__ void __launch_bounds__(kEwThreads, ew_min_blocks<Op, TA, TB, TO, NIN>
                                                         const TB* __restrict__ b, TO* __restrict__ out,
                                                         NdArgs g, int64_t nitems, int64_t cpr, FastDiv cpr_div,
                                                         int a_bc, int b_bc) {
+  pdl_enter();
   if (a_bc || b_bc) {
     rows_loop<true, Op, TC, TA, TB, TO, NIN>(op, a, b, out, g, nitems, cpr, cpr_div, a_bc, b_bc);
   } else {

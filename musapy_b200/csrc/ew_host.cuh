@@ -200,9 +200,9 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
   switch (pl.kind) {
     case EW_CONTIG: {
       const int64_t nvec = g.numel / N;
-      k_ew_contig<Op, TC, TA, TB, TO, NIN><<<grid_for(nvec, kEwThreads * 4), kEwThreads, 0, s>>>(
-          op, a, b, out, g.numel, pl.a_bc, pl.b_bc);
-      return launch_check("ew_contig");
+      const cudaError_t e = launch_pdl(k_ew_contig<Op, TC, TA, TB, TO, NIN>, dim3(grid_for(nvec, kEwThreads * 4)),
+                                       dim3(kEwThreads), 0, s, op, a, b, out, g.numel, pl.a_bc, pl.b_bc);
+      return launch_check_pdl(e, "ew_contig");
     }
     case EW_ROWS: {
       NdArgs na = nd_args(g, NIN);
@@ -213,9 +213,10 @@ int run_typed(const Op& op, const EwReq& r, cudaStream_t s) {
       int64_t blocks = nitems;
       const int64_t cap = (int64_t)sm_count() * kStreamBlocksPerSm;
       if (blocks > cap) blocks = cap;
-      k_ew_rows<Op, TC, TA, TB, TO, NIN><<<(unsigned)(blocks < 1 ? 1 : blocks), kEwThreads, 0, s>>>(
-          op, a, b, out, na, nitems, cpr, FastDiv((uint32_t)(cpr < 0xffffffffLL ? cpr : 1)), pl.a_bc, pl.b_bc);
-      return launch_check("ew_rows");
+      const cudaError_t e = launch_pdl(k_ew_rows<Op, TC, TA, TB, TO, NIN>, dim3((unsigned)(blocks < 1 ? 1 : blocks)),
+                                       dim3(kEwThreads), 0, s, op, a, b, out, na, nitems, cpr,
+                                       FastDiv((uint32_t)(cpr < 0xffffffffLL ? cpr : 1)), pl.a_bc, pl.b_bc);
+      return launch_check_pdl(e, "ew_rows");
     }
     case EW_TILED: {
       if constexpr (ALLOW_TILED) {

@@ -15,6 +15,9 @@ int cuda_check(cudaError_t e, const char* what);
 // (cudaPeekAtLastError) while a reference-ABI wrapper runs, so the caller's own
 // cudaGetLastError() still sees it as with musapy's kernels.
 int launch_check(const char* what);
+// launch_check for a launch made through cudaLaunchKernelEx, whose own return
+// code `e` is checked as well.
+int launch_check_pdl(cudaError_t e, const char* what);
 void set_preserve_last_error(bool on);
 // Multiprocessor count of the current device (cached per device).
 int sm_count();

@@ -482,6 +482,7 @@ MPB_D void fold_segment_scalar(typename P::Acc& acc, const typename P::In* __res
 template <class P>
 __global__ void __launch_bounds__(kRedThreads) k_red_row_warp(const typename P::In* __restrict__ a, void* out,
                                                                RedDev g, RedOut ro, int vec) {
+  pdl_enter();
   constexpr int VEC = 16 / sizeof(typename P::In) > 0 ? 16 / sizeof(typename P::In) : 1;
   const int lane = threadIdx.x & 31;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -514,6 +515,7 @@ template <class P>
 __global__ void __maxnreg__(56) k_red_row_block(const typename P::In* __restrict__ a, void* out,
                                                                 typename P::Acc* __restrict__ scratch, RedDev g,
                                                                 RedOut ro, int64_t chunk, int vec, int partial) {
+  pdl_enter();
   constexpr int VEC = 16 / sizeof(typename P::In) > 0 ? 16 / sizeof(typename P::In) : 1;
   const int S = gridDim.x;
   const int sx = blockIdx.x;
@@ -559,6 +561,7 @@ template <class P>
 __global__ void __launch_bounds__(kRedThreads) k_red_col(const typename P::In* __restrict__ a, void* out,
                                                           typename P::Acc* __restrict__ scratch, RedDev g,
                                                           RedOut ro, int64_t chunk, int partial) {
+  pdl_enter();
   const int sx = blockIdx.y;
   const int64_t f0 = partial ? (int64_t)sx * chunk : 0;
   int64_t f1 = partial ? f0 + chunk : g.L;
@@ -623,6 +626,7 @@ template <class P, int V>
 __global__ void __launch_bounds__(kRedThreads, 4) k_red_col_v(const typename P::In* __restrict__ a, void* out,
                                                                typename P::Acc* __restrict__ scratch, RedDev g,
                                                                RedOut ro, int64_t chunk, int partial) {
+  pdl_enter();
   using In = typename P::In;
   using Acc = typename P::Acc;
   constexpr int B = V * (int)sizeof(In);
@@ -687,6 +691,7 @@ template <class P>
 __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::In* __restrict__ a, void* out,
                                                               const typename P::Acc* __restrict__ part, RedDev g,
                                                               RedOut ro, int S, int layout) {
+  pdl_enter();
   if (layout == 0) {
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -744,6 +749,7 @@ __global__ void __launch_bounds__(kRedThreads) k_red_combine(const typename P::I
 template <class P>
 __global__ void __launch_bounds__(kRedThreads) k_red_gen(const typename P::In* __restrict__ a, void* out, RedDev g,
                                                           RedOut ro) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -802,31 +808,32 @@ int launch_col_v(const typename P::In* a, void* out, typename P::Acc* scratch, c
             partial ? (unsigned)pl.splits : 1u);
   const int64_t chunk = partial ? pl.chunk : 0;
   bool launched = false;
+  cudaError_t e = cudaSuccess;
   if constexpr (SZ == 2) {
     if (pl.colv == 8) {
-      k_red_col_v<P, 8><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      e = launch_pdl(k_red_col_v<P, 8>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, chunk, partial);
       launched = true;
     } else if (pl.colv == 4) {
-      k_red_col_v<P, 4><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      e = launch_pdl(k_red_col_v<P, 4>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, chunk, partial);
       launched = true;
     }
   } else if constexpr (SZ == 4) {
     if (pl.colv == 4) {
-      k_red_col_v<P, 4><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      e = launch_pdl(k_red_col_v<P, 4>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, chunk, partial);
       launched = true;
     } else if (pl.colv == 2) {
-      k_red_col_v<P, 2><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      e = launch_pdl(k_red_col_v<P, 2>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, chunk, partial);
       launched = true;
     }
   } else if constexpr (SZ == 8) {
     if (pl.colv == 2) {
-      k_red_col_v<P, 2><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, chunk, partial);
+      e = launch_pdl(k_red_col_v<P, 2>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, chunk, partial);
       launched = true;
     }
   }
   if (!launched)
     return fail(MPB_ERR_INVALID, "reduce: no column kernel for %d outputs of %d bytes per thread", pl.colv, SZ);
-  return launch_check(partial ? "reduce_col_v_split" : "reduce_col_v");
+  return launch_check_pdl(e, partial ? "reduce_col_v_split" : "reduce_col_v");
 }
 
 template <class P>
@@ -845,43 +852,49 @@ int launch_policy(const RedReq& r, const RedPlan& pl, RedOut ro, cudaStream_t s)
   const int vec = pl.vectorized ? 1 : 0;
   switch (pl.kind) {
     case RK_ROW_WARP:
-      k_red_row_warp<P><<<blocks_for(pl.M * 32, kRedThreads, 32), kRedThreads, 0, s>>>(a, out, g, ro, vec);
-      return launch_check("reduce_row_warp");
+      return launch_check_pdl(launch_pdl(k_red_row_warp<P>, dim3(blocks_for(pl.M * 32, kRedThreads, 32)),
+                                         dim3(kRedThreads), 0, s, a, out, g, ro, vec),
+                              "reduce_row_warp");
     case RK_ROW_BLOCK: {
       dim3 grid(1, (unsigned)(pl.M < 65535 ? pl.M : 65535));
-      k_red_row_block<P><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, 0, vec, 0);
-      return launch_check("reduce_row_block");
+      return launch_check_pdl(
+          launch_pdl(k_red_row_block<P>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, (int64_t)0, vec, 0),
+          "reduce_row_block");
     }
     case RK_ROW_SPLIT: {
       dim3 grid((unsigned)pl.splits, (unsigned)(pl.M < 65535 ? pl.M : 65535));
-      k_red_row_block<P><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, pl.chunk, vec, 1);
-      int rc = launch_check("reduce_row_split");
+      int rc = launch_check_pdl(
+          launch_pdl(k_red_row_block<P>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, pl.chunk, vec, 1),
+          "reduce_row_split");
       if (rc) return rc;
-      k_red_combine<P><<<(unsigned)(pl.M < 65535 ? pl.M : 65535), kRedThreads, 0, s>>>(a, out, scratch, g, ro,
-                                                                                    (int)pl.splits, 2);
-      return launch_check("reduce_row_combine");
+      return launch_check_pdl(launch_pdl(k_red_combine<P>, dim3((unsigned)(pl.M < 65535 ? pl.M : 65535)),
+                                         dim3(kRedThreads), 0, s, a, out, (const Acc*)scratch, g, ro, (int)pl.splits, 2),
+                              "reduce_row_combine");
     }
     case RK_COL:
       if (pl.colv > 1) return launch_col_v<P>(a, out, scratch, g, ro, pl, 0, s);
-      k_red_col<P><<<blocks_for(pl.M, kRedThreads, 64), kRedThreads, 0, s>>>(a, out, scratch, g, ro, 0, 0);
-      return launch_check("reduce_col");
+      return launch_check_pdl(launch_pdl(k_red_col<P>, dim3(blocks_for(pl.M, kRedThreads, 64)), dim3(kRedThreads), 0,
+                                         s, a, out, scratch, g, ro, (int64_t)0, 0),
+                              "reduce_col");
     case RK_COL_SPLIT: {
       int rc;
       if (pl.colv > 1) {
         rc = launch_col_v<P>(a, out, scratch, g, ro, pl, 1, s);
       } else {
         dim3 grid((unsigned)cdiv(pl.M, kRedThreads), (unsigned)pl.splits);
-        k_red_col<P><<<grid, kRedThreads, 0, s>>>(a, out, scratch, g, ro, pl.chunk, 1);
-        rc = launch_check("reduce_col_split");
+        rc = launch_check_pdl(
+            launch_pdl(k_red_col<P>, grid, dim3(kRedThreads), 0, s, a, out, scratch, g, ro, pl.chunk, 1),
+            "reduce_col_split");
       }
       if (rc) return rc;
-      k_red_combine<P><<<blocks_for(pl.M, kRedThreads, 64), kRedThreads, 0, s>>>(a, out, scratch, g, ro,
-                                                                               (int)pl.splits, 1);
-      return launch_check("reduce_col_combine");
+      return launch_check_pdl(launch_pdl(k_red_combine<P>, dim3(blocks_for(pl.M, kRedThreads, 64)),
+                                         dim3(kRedThreads), 0, s, a, out, (const Acc*)scratch, g, ro, (int)pl.splits, 1),
+                              "reduce_col_combine");
     }
     default:
-      k_red_gen<P><<<blocks_for(pl.M * 32, kRedThreads, 32), kRedThreads, 0, s>>>(a, out, g, ro);
-      return launch_check("reduce_gen");
+      return launch_check_pdl(launch_pdl(k_red_gen<P>, dim3(blocks_for(pl.M * 32, kRedThreads, 32)),
+                                         dim3(kRedThreads), 0, s, a, out, g, ro),
+                              "reduce_gen");
   }
 }
 
