@@ -95,6 +95,9 @@ def _plan_at(op, shape, strides, addr, dt, mask):
     # loads for arg reductions), one partial wave, 16 MiB in flight - no split
     (5, (64, 4096, 4096), (1 << 24, 4096, 1), 1 << 20, 10, 0b010, (4, 262144, 4096, 1, 2)),
     (6, (64, 4096, 4096), (1 << 24, 4096, 1), (1 << 20) + 8, 10, 0b010, (4, 262144, 4096, 1, 2)),
+    # half of it (32 planes): 8 MiB in flight would leave the grid
+    # latency-bound, so it is split
+    (5, (32, 4096, 4096), (1 << 24, 4096, 1), 1 << 20, 10, 0b010, (5, 131072, 4096, None, 2)),
     # aligned to 4 bytes only: one per thread, split against the tail wave
     (5, (64, 4096, 4096), (1 << 24, 4096, 1), (1 << 20) + 4, 10, 0b010, (5, 262144, 4096, None, 1)),
     # sum / max over axis 0 of (64, 4096, 4096): 16-byte loads, many waves, no split
